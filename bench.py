@@ -1,0 +1,566 @@
+#!/usr/bin/env python
+"""Benchmark of the fused dequantize + GEMV decode path on B200.
+
+Default workload (the metric's configuration): one
+LLaMA-7B-shaped batch-1 decode token through the hot path = the 224 Q4_0
+projections of 32 layers (q, k, v, o 4096x4096; gate, up 11008x4096; down
+4096x11008) plus the 32000x4096 Q8_0 lm_head, all weights resident in HBM
+(3.78 GB per token, far larger than the 126 MB L2, so no flush is needed).
+Each projection's input is the previous projection's output (x -> q,k,v;
+v -> o; o -> gate, up; up -> down; down -> next layer; -> lm_head), so the
+launches form a real dependency chain.  Attention, RMSNorm, RoPE and SwiGLU
+are the callers' torch ops and are not part of this path.
+
+A step is one token.  ``value`` = tokens/s with inputs resident (the 225
+launches of a token captured once in a CUDA graph with programmatic
+dependent launch, replayed per token), timed with CUDA events, max over
+ranks.  ``e2e`` = the same tokens/s through the reference-facing op API
+(gds_io_ext.fused_dequant_gemv, called exactly as llama.py calls it) with
+the token's input copied host->device and the logits device->host every step.
+
+--impl reference: the reference's path on this box: its CPU path (its dequant
+formula + torch.matmul on all host cores; the oracle port) as ``value``, and
+GdsLLM's own CUDA kernels, compiled unchanged for sm_100a, on the same token
+as ``ref_cuda``.
+
+--gpus N (under torchrun): N independent replicas (weak scaling).
+--config 0: one 11008x4096 Q4_0 GEMV, rotating over copies larger than L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from gdsllm_b200 import synth  # noqa: E402
+
+LAYERS, HIDDEN, FFN, VOCAB = 32, 4096, 11008, 32000
+PROJ = [("q", HIDDEN, HIDDEN), ("k", HIDDEN, HIDDEN), ("v", HIDDEN, HIDDEN), ("o", HIDDEN, HIDDEN),
+        ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
+SRC = {"q": "x", "k": "x", "v": "x", "o": "v", "gate": "o", "up": "o", "down": "up"}
+
+
+def q4_bytes(n, k):
+    return n * (k // 32) * 18
+
+
+def q8_bytes(n, k):
+    return n * (k // 32) * 34
+
+
+def gemv_alg_bytes(n, k, wbytes):
+    return wbytes + 2 * k + 2 * n  # weights + x + y (fp16)
+
+
+LAYER_WBYTES = sum(q4_bytes(n, k) for _, n, k in PROJ)
+TOKEN_WBYTES = LAYERS * LAYER_WBYTES + q8_bytes(VOCAB, HIDDEN)
+TOKEN_ALG_BYTES = (LAYERS * sum(gemv_alg_bytes(n, k, q4_bytes(n, k)) for _, n, k in PROJ)
+                   + gemv_alg_bytes(VOCAB, HIDDEN, q8_bytes(VOCAB, HIDDEN)))
+
+
+def load_peaks():
+    try:
+        p = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.device = torch.device("cuda", self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", device_id=self.device,
+                                    timeout=datetime.timedelta(seconds=120))
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    """nvidia-smi samples every 100 ms; only samples whose timestamp falls
+    inside [start(), stop()] count."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.target = str(device.index)
+        if cvd:
+            ids = [c.strip() for c in cvd.split(",") if c.strip()]
+            if device.index < len(ids):
+                self.target = ids[device.index]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.target],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.5)
+        self.t0 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        t1 = time.time()
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        import datetime
+        sm, smax, reasons, power = [], 0.0, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                if not (self.t0 - 0.05 <= ts <= t1 + 0.05):
+                    continue
+                sm.append(float(f[2]))
+                smax = max(smax, float(f[3]))
+                power.append(float(f[4]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------
+# the token's weights and activations
+
+class Token:
+    """Resident weights of a LLaMA-7B-shaped model (Q4_0 body, Q8_0 lm_head),
+    one uint8 buffer per layer with 4 KB-aligned tensor offsets like the
+    reference's layer files, and preallocated activations."""
+
+    def __init__(self, device, seed=0):
+        self.device = device
+        self.layers = []
+        for li in range(LAYERS):
+            offs, cur = {}, 0
+            for name, n, k in PROJ:
+                offs[name] = (cur, n, k)
+                cur += (q4_bytes(n, k) + 4095) // 4096 * 4096
+            buf = torch.empty(cur, dtype=torch.uint8, device=device)
+            for pi, (name, n, k) in enumerate(PROJ):
+                o = offs[name][0]
+                w = synth.q4_0_weight(n, k, seed=seed * 1000 + li * 8 + pi, device=device)
+                buf[o:o + w.numel()] = w.reshape(-1)
+                del w
+            self.layers.append((buf, offs))
+        self.lm_head = synth.q8_0_weight(VOCAB, HIDDEN, seed=seed * 1000 + 999, device=device)
+        self.x0 = synth.activations(1, HIDDEN, seed=seed + 7, device=device).reshape(-1)
+        self.act = {"x": torch.empty(HIDDEN, dtype=torch.float16, device=device)}
+        for name, n, _ in PROJ:
+            self.act[name] = torch.empty(n, dtype=torch.float16, device=device)
+        self.layer_out = [torch.empty(HIDDEN, dtype=torch.float16, device=device) for _ in range(LAYERS)]
+        self.logits = torch.empty(VOCAB, dtype=torch.float16, device=device)
+
+    def launches(self):
+        """(weight ptr, n, k, x ptr, y ptr, fmt) for the 225 GEMVs of a token."""
+        seq = []
+        x_ptr = self.act["x"].data_ptr()
+        for li, (buf, offs) in enumerate(self.layers):
+            cur = {"x": x_ptr}
+            for name, n, k in PROJ:
+                y = self.layer_out[li] if name == "down" else self.act[name]
+                seq.append((buf.data_ptr() + offs[name][0], n, k, cur[SRC[name]], y.data_ptr(), "q4_0"))
+                cur[name] = y.data_ptr()
+            x_ptr = self.layer_out[li].data_ptr()
+        seq.append((self.lm_head.data_ptr(), VOCAB, HIDDEN, x_ptr, self.logits.data_ptr(), "q8_0"))
+        return seq
+
+
+def run_ours(seq, stream, lib):
+    for w, n, k, x, y, fmt in seq:
+        fn = lib.gdsq_fused_q4_0_gemv if fmt == "q4_0" else lib.gdsq_fused_q8_0_gemv
+        st = fn(w, x, y, n, k, 1, stream)
+        if st:
+            raise RuntimeError(lib.gdsq_last_error().decode())
+
+
+def capture(fn):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(s.cuda_stream)  # warm-up outside capture (sets kernel attributes)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        fn(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, steps, warmup, dist, clocks=None):
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    if clocks:
+        clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    info = clocks.stop() if clocks else None
+    dist.barrier()
+    return dist.max(ms), info
+
+
+def per_launch_times(seq, lib, tokens):
+    """Instrumented eager pass (no PDL): CUDA events around every launch.
+    Returns {(fmt, n, k): [ms, ...]}."""
+    from gdsllm_b200 import capi
+    capi.set_pdl(False)
+    stream = torch.cuda.current_stream()
+    out = {}
+    for _ in range(tokens):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(seq) + 1)]
+        evs[0].record(stream)
+        for i, (w, n, k, x, y, fmt) in enumerate(seq):
+            fn = lib.gdsq_fused_q4_0_gemv if fmt == "q4_0" else lib.gdsq_fused_q8_0_gemv
+            fn(w, x, y, n, k, 1, stream.cuda_stream)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        for i, (_, n, k, _, _, fmt) in enumerate(seq):
+            out.setdefault((fmt, n, k), []).append(evs[i].elapsed_time(evs[i + 1]))
+    return out
+
+
+def e2e_api(tok, ext, steps, warmup, dist):
+    """Tokens/s through gds_io_ext with host buffers: H2D of the token's input
+    and D2H of the logits inside the timed region, every step."""
+    handles = [(ext.handle_from_tensor(buf), offs) for buf, offs in tok.layers]
+    lm = ext.handle_from_tensor(tok.lm_head)
+    x_host = tok.x0.cpu().pin_memory()
+    logits_host = torch.empty(VOCAB, dtype=torch.float16).pin_memory()
+    x_dev = torch.empty(HIDDEN, dtype=torch.float16, device=tok.device)
+
+    def step():
+        x_dev.copy_(x_host, non_blocking=True)
+        x = x_dev.view(1, 1, -1)
+        for h, offs in handles:
+            acts = {"x": x}
+            for name, n, k in PROJ:
+                src = acts[SRC[name]]
+                # llama.py:_fused_dequant_gemv: x.view(-1) -> [1, out] -> unsqueeze(0)
+                acts[name] = ext.fused_dequant_gemv(h, src.view(-1), [n, k], "q4_0", offs[name][0]).unsqueeze(0)
+            x = acts["down"]
+        out = ext.fused_dequant_gemv(lm, x.view(-1), [VOCAB, HIDDEN], "q8_0", 0)
+        logits_host.copy_(out.view(-1), non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    return dist.max(start.elapsed_time(end))
+
+
+# ---------------------------------------------------------------------------
+# CPU path of the reference (dequant formula + torch.matmul), bounded sample
+
+def cpu_reference_path(budget_s: float = 0.0, max_items: int | None = None, frac: float = 1.0):
+    """Times the reference's CPU path -- dequantize with the formula, then
+    torch.matmul in fp32 -- on LLaMA-7B projections generated on the host,
+    one projection per item, cycling over the 7 layer shapes, until
+    ``max_items`` items (or ``budget_s`` seconds).  ``frac`` < 1 uses only the
+    first rows of each projection.  Returns (tok/s, cores, sample, seconds),
+    tok/s scaled by weight bytes to one token."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    items = []
+    for pi, (name, n, k) in enumerate(PROJ):
+        rows = max(1, int(math.ceil(n * frac)))
+        items.append((synth.q4_0_weight(rows, k, seed=pi).numpy(), rows, k))
+    x = synth.activations(1, FFN, seed=3).numpy()
+    done_bytes, t_total, count = 0, 0.0, 0
+    while True:
+        for w, n, k in items:
+            t0 = time.perf_counter()
+            wd = oracle.dequant_q4_0(w).reshape(n, k)
+            oracle.gemv_cpu(wd, x[:, :k])
+            t_total += time.perf_counter() - t0
+            done_bytes += q4_bytes(n, k)
+            count += 1
+            if (max_items and count >= max_items) or (not max_items and t_total >= budget_s
+                                                      and count >= len(items)):
+                tok_s = done_bytes / t_total / TOKEN_WBYTES
+                sample = (f"{count} LLaMA-7B Q4_0 projections"
+                          f"{'' if frac >= 1 else f' (first {frac:.3f} of rows)'} = "
+                          f"{done_bytes / 1e6:.0f} MB of weights, dequantized by the formula "
+                          f"(C, OpenMP) and multiplied with torch.matmul (fp32), scaled by bytes "
+                          f"to one token ({TOKEN_WBYTES / 1e9:.3f} GB)")
+                return tok_s, threads, sample, t_total
+
+
+# ---------------------------------------------------------------------------
+
+def bench_ours(args, dist):
+    from gdsllm_b200 import capi, lib as gdsq_lib
+    peak, peak_kind = load_peaks()
+    lib = gdsq_lib()
+    tok = Token(dist.device, seed=dist.rank)
+    seq = tok.launches()
+
+    capi.set_pdl(True)
+
+    def fn(stream):
+        tok.act["x"].copy_(tok.x0)
+        run_ours(seq, stream, lib)
+
+    g = capture(fn)
+    clocks = ClockSampler(dist.device)
+    ms, clock_info = time_graph(g, args.steps, args.warmup, dist, clocks)
+    tok_s = args.steps * dist.world / (ms / 1e3)
+
+    times = per_launch_times(seq, lib, tokens=min(args.steps, 10))
+    q4_ms = sum(sum(v) for (f, _, _), v in times.items() if f == "q4_0")
+    q4_launches = sum(len(v) for (f, _, _), v in times.items() if f == "q4_0")
+    q4_bytes_total = sum(len(v) * gemv_alg_bytes(n, k, q4_bytes(n, k))
+                         for (f, n, k), v in times.items() if f == "q4_0")
+    achieved = q4_bytes_total / (q4_ms / 1e3) / 1e9
+    per_shape = {f"{f} {n}x{k}": {"us": round(statistics.median(v) * 1e3, 2),
+                                  "gbs": round(gemv_alg_bytes(n, k, (q4_bytes if f == "q4_0" else q8_bytes)(n, k))
+                                               / (statistics.median(v) / 1e3) / 1e9, 1)}
+                 for (f, n, k), v in sorted(times.items())}
+    traffic = None
+    tf = ROOT / "profiles" / "gemv_q4_0_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    import gdsllm_b200
+    e2e_ms = e2e_api(tok, gdsllm_b200.ext(), args.steps, max(3, args.warmup), dist)
+    e2e = {"value": round(args.steps * dist.world / (e2e_ms / 1e3), 2), "unit": "tok/s",
+           "h2d_bytes_per_step": HIDDEN * 2, "d2h_bytes_per_step": VOCAB * 2,
+           "api": "gds_io_ext.fused_dequant_gemv x225 per token, as llama.py calls it"}
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        tps, cores, sample, secs = cpu_reference_path(args.cpu_budget)
+        cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": sample + f"; {secs:.1f} s of CPU time"}
+
+    result = {
+        "metric": "LLaMA-7B Q4_0 batch-1 decode tok/s through the fused dequant-GEMV path "
+                  "(224 Q4_0 projections + Q8_0 lm_head per token)",
+        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded random Q4_0/Q8_0 weights per BASELINE config 0/1 distributions)",
+        "config": {"workload": "config 1: LLaMA-7B-shaped decode token, hot path only, batch 1",
+                   "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
+                   "lm_head": "q8_0", "weight_bytes_per_token": TOKEN_WBYTES,
+                   "l2": "inputs larger than L2 (3.78 GB of weights per step)",
+                   "launch": "CUDA graph of 225 launches, programmatic dependent launch",
+                   "parallelism": f"replicas x{dist.world}"},
+        "gbs": round(TOKEN_ALG_BYTES * tok_s / dist.world / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "gemv_fast_kernel<Q4_0, batch 1>",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic, "launches_timed": q4_launches, "per_shape": per_shape},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": len(seq) * args.steps,
+        "clocks": clock_info,
+    }
+    return result
+
+
+def bench_reference(args, dist):
+    """The reference's path: CPU dequant formula + torch.matmul (value), and
+    GdsLLM's own CUDA kernels on the same token (ref_cuda)."""
+    result = {"impl": "reference", "metric": None}
+    if dist.rank != 0:
+        return None
+    # Each step is one projection of the token (bounded sample); rows are
+    # trimmed so that the K timed steps take about two minutes at most.
+    _, _, _, warm_s = cpu_reference_path(max_items=max(7, args.warmup))
+    per_step = warm_s / max(7, args.warmup)
+    frac = min(1.0, 120.0 / (args.steps * per_step))
+    tps, cores, sample, secs = cpu_reference_path(max_items=args.steps, frac=frac)
+    result.update({
+        "metric": "LLaMA-7B Q4_0 batch-1 decode tok/s through the fused dequant-GEMV path "
+                  "(224 Q4_0 projections + Q8_0 lm_head per token)",
+        "value": round(tps, 4), "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config 1: LLaMA-7B-shaped decode token, hot path only, batch 1",
+                   "step": "one projection of the token (rotating over the 7 layer shapes)"},
+        "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    })
+    # GdsLLM's CUDA kernels (compiled unchanged) on the same token, on this B200.
+    try:
+        from oracle import reference_kernels as refk
+        if refk.available():
+            result["ref_cuda"] = bench_reference_cuda(args, dist, refk)
+    except Exception as e:  # the CPU line above stands on its own
+        result["ref_cuda"] = {"error": str(e)[:200]}
+    return result
+
+
+def bench_reference_cuda(args, dist, refk):
+    tok = Token(dist.device, seed=0)
+    seq = tok.launches()
+    l = refk.lib()
+    lm_fp16 = torch.empty(VOCAB, HIDDEN, dtype=torch.float16, device=dist.device)
+
+    def fn(stream):
+        tok.act["x"].copy_(tok.x0)
+        for w, n, k, x, y, fmt in seq:
+            if fmt == "q4_0":
+                l.ref_fused_q4_0_gemv(w, x, y, n, k, stream)
+            else:
+                # the reference scheduler's lm_head: full dequant + F.linear
+                # (gdsllm/runtime/scheduler.py:54-55,69); torch runs on the
+                # same (current) stream as the ctypes launches.
+                l.ref_dequant_q8_0(w, lm_fp16.data_ptr(), VOCAB * HIDDEN // 32, stream)
+                torch.matmul(tok.layer_out[-1].view(1, -1), lm_fp16.t(), out=tok.logits.view(1, -1))
+
+    g = capture(fn)
+    ms, _ = time_graph(g, args.steps, args.warmup, dist)
+    tps = args.steps / (ms / 1e3)
+    return {"value": round(tps, 2), "unit": "tok/s", "ms_per_step": round(ms / args.steps, 4),
+            "gbs": round(TOKEN_ALG_BYTES * tps / 1e9, 1),
+            "what": "GdsLLM's fused_gemv.cu / gguf_dequant.cu compiled unchanged for sm_100a, same "
+                    "token chain in a CUDA graph; lm_head as the reference scheduler does it "
+                    "(dequant_q8_0 to fp16 + cuBLAS)"}
+
+
+# ---------------------------------------------------------------------------
+
+def bench_config0(args, dist):
+    """One 11008x4096 Q4_0 GEMV, rotating over copies that together exceed L2."""
+    from gdsllm_b200 import capi, lib as gdsq_lib
+    peak, peak_kind = load_peaks()
+    lib = gdsq_lib()
+    n, k = 11008, 4096
+    copies = 8
+    ws = [synth.q4_0_weight(n, k, seed=i, device=dist.device) for i in range(copies)]
+    x = synth.activations(1, k, seed=9, device=dist.device)
+    y = torch.empty(1, n, dtype=torch.float16, device=dist.device)
+    capi.set_pdl(args.pdl)
+
+    def fn(stream):
+        for w in ws:
+            st = lib.gdsq_fused_q4_0_gemv(w.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, 1, stream)
+            if st:
+                raise RuntimeError(lib.gdsq_last_error().decode())
+
+    g = capture(fn)
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dist.device))
+    launches = args.steps * copies
+    us = ms * 1e3 / launches
+    b = gemv_alg_bytes(n, k, q4_bytes(n, k))
+    gbs = b / (us / 1e6) / 1e9
+    return {"metric": "Q4_0 fused dequant-GEMV 11008x4096 batch 1, HBM GB/s", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config 0", "copies": copies, "pdl": bool(args.pdl),
+                       "l2": f"rotating over {copies} weight copies ({copies * q4_bytes(n, k) / 1e6:.0f} MB > L2)"},
+            "us_per_launch": round(us, 3),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind},
+            "gpu_launches": launches, "clocks": clk}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1])
+    ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            res = bench_reference(args, dist)
+        elif args.config == 0:
+            res = bench_config0(args, dist)
+        else:
+            res = bench_ours(args, dist)
+        if dist.rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

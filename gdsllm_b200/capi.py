@@ -1,0 +1,82 @@
+"""Thin torch-tensor front end to the C ABI (include/gdsq.h), via ctypes.
+
+Every function launches on the current CUDA stream of the tensors' device
+and raises ``GdsqError`` for a non-OK status.  Outputs are allocated unless
+``out`` is given (then they are written in place and returned).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._native import check, lib
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _out(out, shape, like):
+    if out is None:
+        return torch.empty(shape, dtype=torch.float16, device=like.device)
+    return out
+
+
+def set_pdl(enable: bool) -> None:
+    check(lib().gdsq_set_pdl(1 if enable else 0), "gdsq_set_pdl")
+
+
+def device_error(device: int = 0, clear: bool = True) -> int:
+    bits = ctypes.c_int(0)
+    check(lib().gdsq_device_error(device, 1 if clear else 0, ctypes.byref(bits)), "gdsq_device_error")
+    return bits.value
+
+
+def dequant_q4_0(raw: torch.Tensor, num_blocks: int | None = None, out=None) -> torch.Tensor:
+    n = raw.numel() // 18 if num_blocks is None else num_blocks
+    out = _out(out, (n * 32,), raw)
+    check(lib().gdsq_dequant_q4_0(_p(raw), _p(out), n, _stream(raw)), "gdsq_dequant_q4_0")
+    return out
+
+
+def dequant_q8_0(raw: torch.Tensor, num_blocks: int | None = None, out=None) -> torch.Tensor:
+    n = raw.numel() // 34 if num_blocks is None else num_blocks
+    out = _out(out, (n * 32,), raw)
+    check(lib().gdsq_dequant_q8_0(_p(raw), _p(out), n, _stream(raw)), "gdsq_dequant_q8_0")
+    return out
+
+
+def dequant_affine_q4(words, scales, biases, in_dim: int, group: int, out=None) -> torch.Tensor:
+    n = words.numel() * 8
+    out = _out(out, (n,), words)
+    check(lib().gdsq_dequant_affine_q4(_p(words), _p(scales), _p(biases), _p(out), n, in_dim, group,
+                                       _stream(words)), "gdsq_dequant_affine_q4")
+    return out
+
+
+def gemv_q4_0(w: torch.Tensor, x: torch.Tensor, n: int, k: int, out=None) -> torch.Tensor:
+    b = x.numel() // k
+    out = _out(out, (b, n), x)
+    check(lib().gdsq_fused_q4_0_gemv(_p(w), _p(x), _p(out), n, k, b, _stream(x)), "gdsq_fused_q4_0_gemv")
+    return out
+
+
+def gemv_q8_0(w: torch.Tensor, x: torch.Tensor, n: int, k: int, out=None) -> torch.Tensor:
+    b = x.numel() // k
+    out = _out(out, (b, n), x)
+    check(lib().gdsq_fused_q8_0_gemv(_p(w), _p(x), _p(out), n, k, b, _stream(x)), "gdsq_fused_q8_0_gemv")
+    return out
+
+
+def gemv_affine_q4(words, scales, biases, x: torch.Tensor, n: int, k: int, group: int,
+                   out=None) -> torch.Tensor:
+    b = x.numel() // k
+    out = _out(out, (b, n), x)
+    check(lib().gdsq_fused_affine_q4_gemv(_p(words), _p(scales), _p(biases), _p(x), _p(out), n, k,
+                                          group, b, _stream(x)), "gdsq_fused_affine_q4_gemv")
+    return out

@@ -1,0 +1,161 @@
+// Device-side helpers shared by every gdsq kernel: inline PTX for mbarriers,
+// 1-D bulk async copies (the TMA engine's untiled path), programmatic
+// dependent launch and the bounded waits that every spin in this library uses.
+//
+// All kernels are compiled for sm_100a only.  Nothing here uses cluster
+// multicast: every bulk load names a single destination CTA.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdsq {
+
+// Kernel-side error word (one per device, in the module's static memory).
+// Kernels OR a bit in and return instead of trapping; the host reads it with
+// gdsq_device_error().  Bits:
+enum : int {
+  kDevErrBarrierTimeout = 1,   // an mbarrier wait on a bulk copy gave up
+  kDevErrBadArgument = 2,      // a launch saw inconsistent arguments
+};
+__device__ int g_device_error;
+
+// Upper bound for any wait on an async copy, in nanoseconds of %globaltimer.
+// A weight tile takes microseconds to arrive; one second means "never".
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes barrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy writes to the same buffer (slot reuse in a ring).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Returns false after
+// kWaitLimitNs without completion; the caller records the error and unwinds.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+// One contiguous global -> shared copy by the bulk-copy engine.  dst, src and
+// bytes must all be multiples of 16.  Completion is signalled on `bar` as
+// transaction bytes.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Same copy with an L2 eviction-priority hint (weights are streamed once).
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, uint32_t bytes,
+                                                   uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Programmatic dependent launch.  Both are no-ops when the kernel was not
+// launched with the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait_primary() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void record_device_error(int bit) { atomicOr(&g_device_error, bit); }
+
+// ---- fp16 bit tricks -------------------------------------------------------
+// The "magic number" conversion: OR-ing a 4-bit value n into the low mantissa
+// bits of fp16 1024.0 (0x6400) gives exactly 1024 + n, because the fp16 ulp in
+// [1024, 2048) is 1.  Subtracting a constant afterwards is exact as well.
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+  uint32_t r;
+  // immLut 0xEA = (a & b) | c
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
+  return r;
+}
+
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) {
+  return *reinterpret_cast<__half2*>(&v);
+}
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t h2_const(float a, float b) {
+  return h2_as_u32(__floats2half2_rn(a, b));
+}
+
+// Unpacks the 8 nibbles of one 32-bit word into 4 half2 values of (n - 8),
+// all exact.  Output pairs (bit positions of the two nibbles):
+//   r[0] = (bits 0-3,  bits 16-19)     r[1] = (bits 4-7,   bits 20-23)
+//   r[2] = (bits 8-11, bits 24-27)     r[3] = (bits 12-15, bits 28-31)
+__device__ __forceinline__ void unpack_nibbles_minus8(uint32_t q, __half2 r[4]) {
+  const uint32_t kMagic = 0x64006400u;
+  const __half2 k1032 = u32_as_h2(0x64086408u);      // 1032.0
+  const __half2 kSixteenth = u32_as_h2(0x2C002C00u);  // 0.0625
+  const __half2 kMinus72 = u32_as_h2(0xD480D480u);    // -72.0
+  const uint32_t q8 = q >> 8;
+  r[0] = __hsub2(u32_as_h2(lop3_and_or(q, 0x000F000Fu, kMagic)), k1032);
+  r[1] = __hfma2(u32_as_h2(lop3_and_or(q, 0x00F000F0u, kMagic)), kSixteenth, kMinus72);
+  r[2] = __hsub2(u32_as_h2(lop3_and_or(q8, 0x000F000Fu, kMagic)), k1032);
+  r[3] = __hfma2(u32_as_h2(lop3_and_or(q8, 0x00F000F0u, kMagic)), kSixteenth, kMinus72);
+}
+
+}  // namespace gdsq

@@ -1,0 +1,539 @@
+// gds_io_ext: the Python op boundary of GdsLLM's decode path, rebuilt on the
+// gdsq C ABI (include/gdsq.h).
+//
+// Mirrors the reference module gdsllm/runtime/gds_bindings.cpp:516-615: the
+// same op names, argument names, defaults, return shapes and RuntimeError
+// conditions, so gdsllm/runtime/llama.py:106-166, qwen_moe.py:20-73 and the
+// schedulers run unchanged when this module is imported in its place.
+//
+// Differences, all additive:
+//   * x may hold B <= 16 rows of K (any shape with numel == B*K); the fused
+//     GEMVs then return [B, N].  B == 1 returns [1, N] as before.
+//   * every op takes a device guard on the handle's device (the reference
+//     launched on whatever device was current).
+//   * kernel launch failures raise instead of printing to stderr.
+//   * bounds of offsets against the handle size and the dtype/device of x and
+//     of the output buffer are checked before launch.
+//   * handle_from_tensor() wraps an existing CUDA tensor as a handle (tests,
+//     synthetic weights); set_pdl() / device_error() expose library controls.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cuda_runtime.h>
+#include <cufile.h>
+#include <dlfcn.h>
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gdsq.h"
+
+namespace py = pybind11;
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// cuFile, resolved at run time so that the module imports on hosts without a
+// GPUDirect Storage stack (reads then go through pread + cudaMemcpy, which is
+// what cuFile's compatibility mode does as well).
+
+struct CuFileApi {
+  bool resolved = false;
+  bool available = false;
+  bool initialized = false;
+  bool driver_open = false;
+  CUfileError_t (*driver_open_fn)() = nullptr;
+  CUfileError_t (*driver_close_fn)() = nullptr;
+  CUfileError_t (*buf_register)(const void*, size_t, int) = nullptr;
+  CUfileError_t (*buf_deregister)(const void*) = nullptr;
+  CUfileError_t (*handle_register)(CUfileHandle_t*, CUfileDescr_t*) = nullptr;
+  void (*handle_deregister)(CUfileHandle_t) = nullptr;
+  ssize_t (*read)(CUfileHandle_t, void*, size_t, off_t, off_t) = nullptr;
+};
+
+CuFileApi g_cufile;
+std::mutex g_cufile_mutex;
+
+void resolve_cufile() {
+  if (g_cufile.resolved) return;
+  g_cufile.resolved = true;
+  void* lib = dlopen("libcufile.so.0", RTLD_NOW | RTLD_GLOBAL);
+  if (!lib) lib = dlopen("libcufile.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!lib) return;
+  auto sym = [&](const char* n) { return dlsym(lib, n); };
+  g_cufile.driver_open_fn = reinterpret_cast<CUfileError_t (*)()>(sym("cuFileDriverOpen"));
+  void* close_fn = sym("cuFileDriverClose_v2");
+  if (!close_fn) close_fn = sym("cuFileDriverClose");
+  g_cufile.driver_close_fn = reinterpret_cast<CUfileError_t (*)()>(close_fn);
+  g_cufile.buf_register =
+      reinterpret_cast<CUfileError_t (*)(const void*, size_t, int)>(sym("cuFileBufRegister"));
+  g_cufile.buf_deregister = reinterpret_cast<CUfileError_t (*)(const void*)>(sym("cuFileBufDeregister"));
+  g_cufile.handle_register =
+      reinterpret_cast<CUfileError_t (*)(CUfileHandle_t*, CUfileDescr_t*)>(sym("cuFileHandleRegister"));
+  g_cufile.handle_deregister = reinterpret_cast<void (*)(CUfileHandle_t)>(sym("cuFileHandleDeregister"));
+  g_cufile.read = reinterpret_cast<ssize_t (*)(CUfileHandle_t, void*, size_t, off_t, off_t)>(sym("cuFileRead"));
+  g_cufile.available = g_cufile.driver_open_fn && g_cufile.driver_close_fn && g_cufile.buf_register &&
+                       g_cufile.buf_deregister && g_cufile.handle_register &&
+                       g_cufile.handle_deregister && g_cufile.read;
+}
+
+// gdsllm/runtime/gds_io.cu:53-69: open the driver once; failure is not fatal.
+void gds_init() {
+  std::lock_guard<std::mutex> lock(g_cufile_mutex);
+  if (g_cufile.initialized) return;
+  resolve_cufile();
+  if (g_cufile.available) {
+    CUfileError_t st = g_cufile.driver_open_fn();
+    g_cufile.driver_open = st.err == CU_FILE_SUCCESS;
+    if (!g_cufile.driver_open)
+      fprintf(stderr, "gds_io_ext: cuFileDriverOpen returned %d; reads use the compatibility path\n",
+              static_cast<int>(st.err));
+  }
+  g_cufile.initialized = true;
+}
+
+// gdsllm/runtime/gds_io.cu:71-78
+void gds_shutdown() {
+  std::lock_guard<std::mutex> lock(g_cufile_mutex);
+  if (!g_cufile.initialized) return;
+  if (g_cufile.driver_open) g_cufile.driver_close_fn();
+  g_cufile.driver_open = false;
+  g_cufile.initialized = false;
+}
+
+bool gds_is_driver_open() { return g_cufile.driver_open; }
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+
+// A device buffer that weights live in.  Either owned (cudaMalloc, 4 KB
+// rounded, optionally registered with cuFile: gdsllm/runtime/gds_io.cu:93-131)
+// or a view of a torch tensor that it keeps alive.
+class GdsBufferHandle {
+ public:
+  static std::shared_ptr<GdsBufferHandle> allocate(size_t size, int device_id) {
+    auto h = std::shared_ptr<GdsBufferHandle>(new GdsBufferHandle());
+    h->device_id_ = device_id;
+    h->size_ = ((size + 4095) / 4096) * 4096;
+    if (h->size_ == 0) h->size_ = 4096;
+    c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_id));
+    check_cuda(cudaMalloc(&h->ptr_, h->size_), "gds_alloc: cudaMalloc");
+    h->owned_ = true;
+    if (g_cufile.driver_open) {
+      CUfileError_t st = g_cufile.buf_register(h->ptr_, h->size_, 0);
+      h->registered_ = st.err == CU_FILE_SUCCESS;
+    }
+    return h;
+  }
+
+  static std::shared_ptr<GdsBufferHandle> wrap(const torch::Tensor& t) {
+    if (!t.is_cuda()) throw std::runtime_error("handle_from_tensor: tensor must be on a CUDA device");
+    if (!t.is_contiguous()) throw std::runtime_error("handle_from_tensor: tensor must be contiguous");
+    auto h = std::shared_ptr<GdsBufferHandle>(new GdsBufferHandle());
+    h->tensor_ = t;
+    h->ptr_ = t.data_ptr();
+    h->size_ = static_cast<size_t>(t.numel()) * t.element_size();
+    h->device_id_ = t.get_device();
+    return h;
+  }
+
+  ~GdsBufferHandle() {
+    if (owned_ && ptr_) {
+      if (registered_ && g_cufile.available) g_cufile.buf_deregister(ptr_);
+      int prev = 0;
+      cudaGetDevice(&prev);
+      cudaSetDevice(device_id_);
+      cudaFree(ptr_);
+      cudaSetDevice(prev);
+    }
+  }
+
+  GdsBufferHandle(const GdsBufferHandle&) = delete;
+  GdsBufferHandle& operator=(const GdsBufferHandle&) = delete;
+
+  void* dev_ptr() const { return ptr_; }
+  size_t size() const { return size_; }
+  int device_id() const { return device_id_; }
+  bool registered() const { return registered_; }
+
+ private:
+  GdsBufferHandle() = default;
+  void* ptr_ = nullptr;
+  size_t size_ = 0;
+  int device_id_ = 0;
+  bool registered_ = false;
+  bool owned_ = false;
+  torch::Tensor tensor_;
+};
+
+using Handle = std::shared_ptr<GdsBufferHandle>;
+
+// Reads `size` bytes at `file_offset` into the buffer at `buf_offset`
+// (gdsllm/runtime/gds_io.cu:135-191).  cuFile first; if the file cannot be
+// registered or the read fails, a pread + cudaMemcpy loop.
+ssize_t gds_read(GdsBufferHandle& buf, const std::string& path, size_t size, off_t file_offset,
+                 off_t buf_offset) {
+  if (!buf.dev_ptr()) throw std::runtime_error("gds_read: invalid buffer");
+  if (static_cast<size_t>(buf_offset) + size > buf.size())
+    throw std::runtime_error("gds_read: read would exceed buffer size");
+  if (size == 0) return 0;
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(buf.device_id()));
+  if (g_cufile.available && g_cufile.initialized) {
+    int fd = open(path.c_str(), O_RDONLY | O_DIRECT);
+    if (fd < 0) fd = open(path.c_str(), O_RDONLY);
+    if (fd < 0) throw std::runtime_error("gds_read: cannot open file '" + path + "': " + strerror(errno));
+    CUfileDescr_t descr;
+    memset(&descr, 0, sizeof(descr));
+    descr.handle.fd = fd;
+    descr.type = CU_FILE_HANDLE_TYPE_OPAQUE_FD;
+    CUfileHandle_t fh;
+    CUfileError_t st = g_cufile.handle_register(&fh, &descr);
+    if (st.err == CU_FILE_SUCCESS) {
+      ssize_t n = g_cufile.read(fh, buf.dev_ptr(), size, file_offset, buf_offset);
+      g_cufile.handle_deregister(fh);
+      close(fd);
+      if (n >= 0) return n;
+    } else {
+      close(fd);
+    }
+  }
+  int fd = open(path.c_str(), O_RDONLY);
+  if (fd < 0) throw std::runtime_error("gds_read: cannot open file '" + path + "': " + strerror(errno));
+  const size_t kChunk = 16u << 20;
+  void* staging = nullptr;
+  cudaError_t e = cudaMallocHost(&staging, std::min(size, kChunk));
+  if (e != cudaSuccess) {
+    close(fd);
+    check_cuda(e, "gds_read: cudaMallocHost");
+  }
+  size_t done = 0;
+  while (done < size) {
+    const size_t want = std::min(kChunk, size - done);
+    ssize_t n = pread(fd, staging, want, file_offset + static_cast<off_t>(done));
+    if (n <= 0) break;
+    e = cudaMemcpy(static_cast<char*>(buf.dev_ptr()) + buf_offset + done, staging, n, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) break;
+    done += static_cast<size_t>(n);
+  }
+  cudaFreeHost(staging);
+  close(fd);
+  check_cuda(e, "gds_read: cudaMemcpy");
+  return static_cast<ssize_t>(done);
+}
+
+torch::Dtype parse_dtype(const std::string& s) {
+  if (s == "float16" || s == "half") return torch::kFloat16;
+  if (s == "float32" || s == "float") return torch::kFloat32;
+  if (s == "bfloat16") return torch::kBFloat16;
+  if (s == "int8") return torch::kInt8;
+  if (s == "int32" || s == "int") return torch::kInt32;
+  throw std::runtime_error("Unsupported dtype: " + s);
+}
+
+void raise_status(int status, const char* op) {
+  if (status == GDSQ_OK) return;
+  std::string msg = std::string(op) + ": " + gdsq_status_string(status);
+  const char* detail = gdsq_last_error();
+  if (detail && *detail) msg += std::string(" (") + detail + ")";
+  throw std::runtime_error(msg);
+}
+
+void require_handle(const Handle& h, const char* op) {
+  if (!h || !h->dev_ptr()) throw std::runtime_error(std::string(op) + ": invalid buffer handle");
+}
+
+void require_range(const Handle& h, int64_t offset, int64_t bytes, const char* op, const char* what) {
+  if (offset < 0 || bytes < 0 || static_cast<uint64_t>(offset) + static_cast<uint64_t>(bytes) > h->size())
+    throw std::runtime_error(std::string(op) + ": " + what + " [" + std::to_string(offset) + ", +" +
+                             std::to_string(bytes) + ") exceeds buffer size " + std::to_string(h->size()));
+}
+
+const char* at_offset(const Handle& h, int64_t offset) {
+  return static_cast<const char*>(h->dev_ptr()) + offset;
+}
+
+// Activation checks shared by both fused GEMVs.  Returns the batch count.
+int check_activation(const torch::Tensor& x, int64_t in_dim, const Handle& h, const char* op) {
+  if (!x.is_cuda() || x.get_device() != h->device_id())
+    throw std::runtime_error(std::string(op) + ": x must be a CUDA tensor on device " +
+                             std::to_string(h->device_id()));
+  if (x.scalar_type() != torch::kFloat16)
+    throw std::runtime_error(std::string(op) + ": x must be float16");
+  const int64_t n = x.numel();
+  if (in_dim == 0 || n == in_dim) return 1;
+  if (n % in_dim != 0 || n / in_dim > GDSQ_MAX_BATCH)
+    throw std::runtime_error(std::string(op) + ": input size " + std::to_string(n) + " != in_dim " +
+                             std::to_string(in_dim));
+  return static_cast<int>(n / in_dim);
+}
+
+torch::Tensor prepare_output(c10::optional<torch::Tensor> out, const std::vector<int64_t>& shape,
+                             int64_t numel, const Handle& h, const char* op) {
+  if (out.has_value()) {
+    torch::Tensor o = out.value();
+    if (o.numel() < numel)
+      throw std::runtime_error(std::string(op) + ": scratch buffer too small (" + std::to_string(o.numel()) +
+                               " < " + std::to_string(numel) + ")");
+    if (!o.is_cuda() || o.get_device() != h->device_id() || o.scalar_type() != torch::kFloat16 ||
+        !o.is_contiguous())
+      throw std::runtime_error(std::string(op) + ": scratch must be a contiguous float16 CUDA tensor on device " +
+                               std::to_string(h->device_id()));
+    return o.flatten().slice(0, 0, numel).view(shape);
+  }
+  auto opts = torch::TensorOptions().dtype(torch::kFloat16).device(torch::kCUDA, h->device_id());
+  return torch::empty(shape, opts);
+}
+
+void* current_stream(const Handle& h) {
+  return static_cast<void*>(
+      at::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(h->device_id())).stream());
+}
+
+// ---------------------------------------------------------------------------
+// Load / view ops (gdsllm/runtime/gds_bindings.cpp:95-247)
+
+Handle py_load_file(const std::string& path, int64_t size_bytes, int device_id) {
+  auto h = GdsBufferHandle::allocate(size_bytes, device_id);
+  ssize_t n = gds_read(*h, path, size_bytes, 0, 0);
+  if (n < size_bytes)
+    throw std::runtime_error("py_load_file: expected " + std::to_string(size_bytes) + " bytes, got " +
+                             std::to_string(n));
+  return h;
+}
+
+Handle py_load_file_region(const std::string& path, int64_t size_bytes, int64_t file_offset,
+                           int device_id) {
+  auto h = GdsBufferHandle::allocate(size_bytes, device_id);
+  ssize_t n = gds_read(*h, path, size_bytes, file_offset, 0);
+  if (n < size_bytes)
+    throw std::runtime_error("py_load_file_region: expected " + std::to_string(size_bytes) +
+                             " bytes, got " + std::to_string(n));
+  return h;
+}
+
+py::tuple py_load_expert(const std::string& path, int64_t w_off, int64_t w_size, int64_t s_off,
+                         int64_t s_size, int64_t b_off, int64_t b_size, int device_id) {
+  auto h = GdsBufferHandle::allocate(w_size + s_size + b_size, device_id);
+  if (gds_read(*h, path, w_size, w_off, 0) < w_size)
+    throw std::runtime_error("py_load_expert: short read on weight");
+  if (gds_read(*h, path, s_size, s_off, w_size) < s_size)
+    throw std::runtime_error("py_load_expert: short read on scale");
+  if (gds_read(*h, path, b_size, b_off, w_size + s_size) < b_size)
+    throw std::runtime_error("py_load_expert: short read on bias");
+  return py::make_tuple(h, static_cast<int64_t>(0), w_size, w_size + s_size);
+}
+
+torch::Tensor view_of(const Handle& h, std::vector<int64_t> shape, const std::string& dtype,
+                      int64_t offset) {
+  auto opts = torch::TensorOptions().dtype(parse_dtype(dtype)).device(torch::kCUDA, h->device_id());
+  void* ptr = static_cast<char*>(h->dev_ptr()) + offset;
+  Handle keep = h;
+  return torch::from_blob(ptr, shape, [keep](void*) {}, opts);
+}
+
+torch::Tensor py_view_tensor(Handle h, std::vector<int64_t> shape, const std::string& dtype,
+                             int64_t offset) {
+  require_handle(h, "py_view_tensor");
+  return view_of(h, std::move(shape), dtype, offset);
+}
+
+torch::Tensor py_load_tensor(const std::string& path, std::vector<int64_t> shape, const std::string& dtype,
+                             int64_t file_offset, int64_t size_bytes, int device_id) {
+  auto h = GdsBufferHandle::allocate(size_bytes, device_id);
+  ssize_t n = gds_read(*h, path, size_bytes, file_offset, 0);
+  if (n < size_bytes)
+    throw std::runtime_error("py_load_tensor: expected " + std::to_string(size_bytes) + " bytes, got " +
+                             std::to_string(n));
+  return view_of(h, std::move(shape), dtype, 0);
+}
+
+// ---------------------------------------------------------------------------
+// Compute ops
+
+// gdsllm/runtime/gds_bindings.cpp:255-314
+torch::Tensor py_dequant_gguf(Handle h, std::vector<int64_t> shape, const std::string& gguf_type,
+                              int64_t offset, c10::optional<torch::Tensor> output) {
+  const char* op = "py_dequant_gguf";
+  require_handle(h, op);
+  int64_t numel = 1;
+  for (auto s : shape) numel *= s;
+  if (numel % 32 != 0)
+    throw std::runtime_error(
+        "py_dequant_gguf: total elements must be a multiple of 32 (block size), got " + std::to_string(numel));
+  const int64_t blocks = numel / 32;
+  int64_t block_bytes;
+  if (gguf_type == "q4_0") block_bytes = 18;
+  else if (gguf_type == "q8_0") block_bytes = 34;
+  else throw std::runtime_error("py_dequant_gguf: unsupported type '" + gguf_type + "'");
+  require_range(h, offset, blocks * block_bytes, op, "weight bytes");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(h->device_id()));
+  torch::Tensor out = prepare_output(output, shape, numel, h, op);
+  const int st = gguf_type == "q4_0"
+                     ? gdsq_dequant_q4_0(at_offset(h, offset), out.data_ptr(), blocks, current_stream(h))
+                     : gdsq_dequant_q8_0(at_offset(h, offset), out.data_ptr(), blocks, current_stream(h));
+  raise_status(st, op);
+  return out;
+}
+
+// gdsllm/runtime/gds_bindings.cpp:333-387
+torch::Tensor py_fused_dequant_gemv(Handle h, torch::Tensor x, std::vector<int64_t> weight_shape,
+                                    const std::string& gguf_type, int64_t offset) {
+  const char* op = "py_fused_dequant_gemv";
+  require_handle(h, op);
+  if (weight_shape.size() != 2)
+    throw std::runtime_error("py_fused_dequant_gemv: weight_shape must be [out_dim, in_dim]");
+  const int64_t out_dim = weight_shape[0];
+  const int64_t in_dim = weight_shape[1];
+  if (in_dim % 32 != 0)
+    throw std::runtime_error("py_fused_dequant_gemv: in_dim must be a multiple of 32, got " +
+                             std::to_string(in_dim));
+  int64_t block_bytes;
+  if (gguf_type == "q4_0") block_bytes = 18;
+  else if (gguf_type == "q8_0") block_bytes = 34;
+  else throw std::runtime_error("py_fused_dequant_gemv: unsupported type '" + gguf_type + "'");
+  const int batch = check_activation(x, in_dim, h, op);
+  require_range(h, offset, out_dim * (in_dim / 32) * block_bytes, op, "weight bytes");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(h->device_id()));
+  torch::Tensor xc = x.contiguous();
+  auto opts = torch::TensorOptions().dtype(torch::kFloat16).device(torch::kCUDA, h->device_id());
+  torch::Tensor out = torch::empty({batch, out_dim}, opts);
+  const int st = gguf_type == "q4_0"
+                     ? gdsq_fused_q4_0_gemv(at_offset(h, offset), xc.data_ptr(), out.data_ptr(),
+                                            static_cast<int>(out_dim), static_cast<int>(in_dim), batch,
+                                            current_stream(h))
+                     : gdsq_fused_q8_0_gemv(at_offset(h, offset), xc.data_ptr(), out.data_ptr(),
+                                            static_cast<int>(out_dim), static_cast<int>(in_dim), batch,
+                                            current_stream(h));
+  raise_status(st, op);
+  return out;
+}
+
+// gdsllm/runtime/gds_bindings.cpp:404-457
+torch::Tensor py_dequant_affine_q4(Handle h, std::vector<int64_t> weight_shape, int64_t weight_offset,
+                                   int64_t scale_offset, int64_t bias_offset, int group_size,
+                                   c10::optional<torch::Tensor> output) {
+  const char* op = "py_dequant_affine_q4";
+  require_handle(h, op);
+  if (weight_shape.size() < 2)
+    throw std::runtime_error("py_dequant_affine_q4: weight_shape must have >= 2 dims");
+  int64_t numel = 1;
+  for (auto s : weight_shape) numel *= s;
+  const int64_t in_dim = weight_shape.back();
+  if (group_size <= 0 || in_dim % group_size != 0 || group_size % 8 != 0)
+    throw std::runtime_error("py_dequant_affine_q4: in_dim " + std::to_string(in_dim) +
+                             " must be a multiple of group_size " + std::to_string(group_size) +
+                             " (itself a multiple of 8)");
+  require_range(h, weight_offset, numel / 2, op, "packed weights");
+  require_range(h, scale_offset, numel / group_size * 2, op, "scales");
+  require_range(h, bias_offset, numel / group_size * 2, op, "biases");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(h->device_id()));
+  torch::Tensor out = prepare_output(output, weight_shape, numel, h, op);
+  const int st = gdsq_dequant_affine_q4(at_offset(h, weight_offset), at_offset(h, scale_offset),
+                                        at_offset(h, bias_offset), out.data_ptr(), numel,
+                                        static_cast<int>(in_dim), group_size, current_stream(h));
+  raise_status(st, op);
+  return out;
+}
+
+// gdsllm/runtime/gds_bindings.cpp:466-512
+torch::Tensor py_fused_affine_q4_gemv(Handle h, torch::Tensor x, std::vector<int64_t> weight_shape,
+                                      int64_t weight_offset, int64_t scale_offset, int64_t bias_offset,
+                                      int group_size) {
+  const char* op = "py_fused_affine_q4_gemv";
+  require_handle(h, op);
+  if (weight_shape.size() != 2)
+    throw std::runtime_error("py_fused_affine_q4_gemv: weight_shape must be [out_dim, in_dim]");
+  const int64_t out_dim = weight_shape[0];
+  const int64_t in_dim = weight_shape[1];
+  if (group_size <= 0 || in_dim % group_size != 0 || group_size % 8 != 0)
+    throw std::runtime_error("py_fused_affine_q4_gemv: in_dim " + std::to_string(in_dim) +
+                             " must be a multiple of group_size " + std::to_string(group_size) +
+                             " (itself a multiple of 8)");
+  const int batch = check_activation(x, in_dim, h, op);
+  require_range(h, weight_offset, out_dim * in_dim / 2, op, "packed weights");
+  require_range(h, scale_offset, out_dim * (in_dim / group_size) * 2, op, "scales");
+  require_range(h, bias_offset, out_dim * (in_dim / group_size) * 2, op, "biases");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(h->device_id()));
+  torch::Tensor xc = x.contiguous();
+  auto opts = torch::TensorOptions().dtype(torch::kFloat16).device(torch::kCUDA, h->device_id());
+  torch::Tensor out = torch::empty({batch, out_dim}, opts);
+  const int st = gdsq_fused_affine_q4_gemv(at_offset(h, weight_offset), at_offset(h, scale_offset),
+                                           at_offset(h, bias_offset), xc.data_ptr(), out.data_ptr(),
+                                           static_cast<int>(out_dim), static_cast<int>(in_dim), group_size,
+                                           batch, current_stream(h));
+  raise_status(st, op);
+  return out;
+}
+
+int py_device_error(int device, bool clear) {
+  int bits = 0;
+  raise_status(gdsq_device_error(device, clear ? 1 : 0, &bits), "device_error");
+  return bits;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(gds_io_ext, m) {
+  m.doc() = "GdsLLM decode-path op boundary on the gdsq sm_100a kernels (B200)";
+  m.attr("backend") = "gdsq-sm100a";
+  m.attr("gdsq_version") = gdsq_version();
+
+  m.def("init", &gds_init, "Initialize the cuFile driver. Call once at startup.");
+  m.def("shutdown", &gds_shutdown, "Shut down the cuFile driver. Call once at exit.");
+  m.def("is_driver_open", &gds_is_driver_open, "Returns True if cuFile driver opened successfully.");
+
+  py::class_<GdsBufferHandle, Handle>(m, "GdsBufferHandle", "Handle to a CUDA buffer holding weights.")
+      .def_property_readonly("size", &GdsBufferHandle::size)
+      .def_property_readonly("device_id", &GdsBufferHandle::device_id)
+      .def_property_readonly("registered", &GdsBufferHandle::registered)
+      .def_property_readonly("data_ptr", [](const GdsBufferHandle& h) {
+        return reinterpret_cast<uintptr_t>(h.dev_ptr());
+      });
+
+  m.def("load_file", &py_load_file, "Load an entire file into a CUDA buffer.", py::arg("filepath"),
+        py::arg("size_bytes"), py::arg("device_id") = 0);
+  m.def("load_file_region", &py_load_file_region, "Load a contiguous file region into a CUDA buffer.",
+        py::arg("filepath"), py::arg("size_bytes"), py::arg("file_offset"), py::arg("device_id") = 0);
+  m.def("load_expert", &py_load_expert, "Load one expert's weight+scale+bias into one CUDA buffer.",
+        py::arg("filepath"), py::arg("w_file_offset"), py::arg("w_size"), py::arg("s_file_offset"),
+        py::arg("s_size"), py::arg("b_file_offset"), py::arg("b_size"), py::arg("device_id") = 0);
+  m.def("view_tensor", &py_view_tensor, "A torch.Tensor view into a GdsBufferHandle at an offset.",
+        py::arg("handle"), py::arg("shape"), py::arg("dtype"), py::arg("offset"));
+  m.def("load_tensor", &py_load_tensor, "Load a file region directly as a CUDA tensor.", py::arg("filepath"),
+        py::arg("shape"), py::arg("dtype") = "float16", py::arg("file_offset") = 0, py::arg("size_bytes") = 0,
+        py::arg("device_id") = 0);
+
+  m.def("dequant_gguf", &py_dequant_gguf, "Dequantize GGUF Q4_0/Q8_0 blocks from a buffer to fp16.",
+        py::arg("handle"), py::arg("shape"), py::arg("gguf_type"), py::arg("offset"),
+        py::arg("output") = py::none());
+  m.def("fused_dequant_gemv", &py_fused_dequant_gemv, "Fused dequant + GEMV for Q4_0/Q8_0 (decode).",
+        py::arg("handle"), py::arg("x"), py::arg("weight_shape"), py::arg("gguf_type"), py::arg("offset"));
+  m.def("dequant_affine_q4", &py_dequant_affine_q4, "Dequantize affine Q4 (uint32 + scales + biases) to fp16.",
+        py::arg("handle"), py::arg("weight_shape"), py::arg("weight_offset"), py::arg("scale_offset"),
+        py::arg("bias_offset"), py::arg("group_size"), py::arg("output") = py::none());
+  m.def("fused_affine_q4_gemv", &py_fused_affine_q4_gemv, "Fused affine Q4 dequant + GEMV (decode).",
+        py::arg("handle"), py::arg("x"), py::arg("weight_shape"), py::arg("weight_offset"),
+        py::arg("scale_offset"), py::arg("bias_offset"), py::arg("group_size"));
+
+  m.def("handle_from_tensor", &GdsBufferHandle::wrap,
+        "Wrap a contiguous CUDA tensor as a GdsBufferHandle (the tensor stays alive with the handle).",
+        py::arg("tensor"));
+  m.def("set_pdl", [](bool on) { gdsq_set_pdl(on ? 1 : 0); },
+        "Enable programmatic dependent launch for the GEMV kernels.", py::arg("enable"));
+  m.def("device_error", &py_device_error, "Read (and optionally clear) the kernel-side error word.",
+        py::arg("device") = 0, py::arg("clear") = true);
+}

@@ -1,0 +1,112 @@
+/*
+ * gdsq — C ABI of the B200 (sm_100a) fused dequantize + GEMV library.
+ *
+ * Plain pointers and sizes only: no torch, no CUDA types.  Every pointer
+ * argument is a device pointer unless stated otherwise; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Every entry
+ * point is asynchronous with respect to the host, returns GDSQ_OK or an error
+ * code, and never aborts the process.  The text of the last error on the
+ * calling thread is available from gdsq_last_error().
+ *
+ * Weight layouts are the reference's packed layouts, unchanged:
+ *   GGUF Q4_0  [N][K/32] blocks of 18 B: fp16 d, 16 bytes of nibbles;
+ *              w[j] = d*((qs[j] & 15) - 8), w[j+16] = d*((qs[j] >> 4) - 8)
+ *              (gdsllm/runtime/gguf_dequant.cu:96-107)
+ *   GGUF Q8_0  [N][K/32] blocks of 34 B: fp16 d, 32 int8; w[i] = d*qs[i]
+ *              (gdsllm/runtime/gguf_dequant.cu:52-57)
+ *   affine Q4  weight uint32 [N][K/8] (8 nibbles, LSB first), fp16 scales and
+ *              biases [N][K/group]; w = fma(nibble, scale, bias)
+ *              (gdsllm/runtime/affine_q4_dequant.cu:54-56, .h:3-12)
+ *
+ * Activations x are fp16 [batch][K] (row-major, contiguous), outputs y are
+ * fp16 [batch][N].  batch = 1 reproduces the reference's batch-1 ops; the
+ * reference has no batch > 1 form.
+ */
+#ifndef GDSQ_H
+#define GDSQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDSQ_API __attribute__((visibility("default")))
+#else
+#define GDSQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gdsq_status {
+  GDSQ_OK = 0,
+  GDSQ_ERR_INVALID_VALUE = 1, /* null pointer, bad shape or size */
+  GDSQ_ERR_MISALIGNED = 2,    /* pointer alignment the format needs is missing */
+  GDSQ_ERR_UNSUPPORTED = 3,   /* valid input this build has no kernel for */
+  GDSQ_ERR_CUDA = 4,          /* a CUDA runtime call failed (see gdsq_last_error) */
+};
+
+#define GDSQ_MAX_BATCH 16
+
+/* Library version, major*10000 + minor*100 + patch. */
+GDSQ_API int gdsq_version(void);
+
+/* Static description of a status code. */
+GDSQ_API const char* gdsq_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+GDSQ_API const char* gdsq_last_error(void);
+
+/* Reads the device-side error word of `device` (bit 1: a bounded wait on an
+ * async copy gave up; bit 2: a kernel rejected its arguments).  Synchronises
+ * the device.  clear != 0 resets the word afterwards. */
+GDSQ_API int gdsq_device_error(int device, int clear, int* out_bits);
+
+/* Programmatic dependent launch for the GEMV kernels (default off).  When on,
+ * a GEMV launched right after another kernel may start streaming its WEIGHTS
+ * before that kernel finishes; activations and outputs are only touched
+ * after it completes.  Turn it on only when no earlier kernel in the stream
+ * writes weight memory. */
+GDSQ_API int gdsq_set_pdl(int enable);
+
+/* ---- Dequantization to fp16 ------------------------------------------- */
+
+/* Replaces launch_dequant_q4_0 (gdsllm/runtime/gguf_dequant.h:26-27).
+ * src: num_blocks * 18 bytes (2-byte aligned); dst: num_blocks * 32 fp16. */
+GDSQ_API int gdsq_dequant_q4_0(const void* src, void* dst, uint64_t num_blocks, void* stream);
+
+/* Replaces launch_dequant_q8_0 (gdsllm/runtime/gguf_dequant.h:19-20).
+ * src: num_blocks * 34 bytes (2-byte aligned); dst: num_blocks * 32 fp16. */
+GDSQ_API int gdsq_dequant_q8_0(const void* src, void* dst, uint64_t num_blocks, void* stream);
+
+/* Replaces launch_dequant_affine_q4 (gdsllm/runtime/affine_q4_dequant.h:29-32).
+ * weight: num_elements/8 uint32 (4-byte aligned); scales, biases:
+ * num_elements/group_size fp16; dst: num_elements fp16.  in_dim must be a
+ * multiple of group_size and group_size a multiple of 8. */
+GDSQ_API int gdsq_dequant_affine_q4(const void* weight, const void* scales, const void* biases, void* dst,
+                           uint64_t num_elements, int in_dim, int group_size, void* stream);
+
+/* ---- Fused dequantize + matrix-vector product ------------------------- */
+
+/* Replaces launch_fused_q4_0_gemv (gdsllm/runtime/fused_gemv.h:23-25).
+ * y[b][n] = fp16( sum_k W[n][k] * x[b][k] ) for b < batch (1..16).
+ * in_dim % 32 == 0; weight 2-byte aligned (16-byte aligned with
+ * in_dim % 256 == 0 takes the bulk-copy fast path). */
+GDSQ_API int gdsq_fused_q4_0_gemv(const void* weight, const void* x, void* y, int out_dim, int in_dim,
+                         int batch, void* stream);
+
+/* Replaces launch_fused_q8_0_gemv (gdsllm/runtime/fused_gemv.h:29-31). */
+GDSQ_API int gdsq_fused_q8_0_gemv(const void* weight, const void* x, void* y, int out_dim, int in_dim,
+                         int batch, void* stream);
+
+/* Replaces launch_fused_affine_q4_gemv (gdsllm/runtime/affine_q4_dequant.h:41-44).
+ * weight [out_dim][in_dim/8] uint32, scales/biases [out_dim][in_dim/group_size]. */
+GDSQ_API int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void* biases,
+                              const void* x, void* y, int out_dim, int in_dim, int group_size,
+                              int batch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDSQ_H */

@@ -1,0 +1,106 @@
+"""CPU checks of the native boundary: the C-ABI library loads and exports
+every symbol include/gdsq.h declares, the binding exports every op name of
+the reference module, and argument validation fails cleanly without
+touching a GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import gdsllm_b200
+from gdsllm_b200._native import GdsqError, check, lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+# Every name the reference binding registers (gdsllm/runtime/gds_bindings.cpp:516-615).
+REFERENCE_OPS = ["init", "shutdown", "is_driver_open", "GdsBufferHandle", "load_file",
+                 "load_file_region", "load_expert", "view_tensor", "load_tensor", "dequant_gguf",
+                 "fused_dequant_gemv", "dequant_affine_q4", "fused_affine_q4_gemv"]
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"GDSQ_API\s+[\w\s\*]+?\b(gdsq_\w+)\s*\(", h.read_text()))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    syms = declared_symbols()
+    assert len(syms) >= 11
+    l = lib()
+    for s in syms:
+        assert hasattr(l, s), f"{s} declared in include/ but not exported"
+
+
+def test_exported_symbols_are_exactly_the_declared_ones():
+    import subprocess
+    from gdsllm_b200.build import LIB_PATH
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = sorted(l.split()[-1] for l in out.splitlines() if l.split()[-1].startswith("gdsq_"))
+    assert exported == declared_symbols()
+
+
+def test_binding_has_the_reference_op_names():
+    m = gdsllm_b200.ext()
+    for name in REFERENCE_OPS:
+        assert hasattr(m, name), name
+    assert m.backend == "gdsq-sm100a"
+
+
+def test_install_as_reference_module():
+    import sys
+    mod = gdsllm_b200.install_as_reference_module("gdsq_test_alias.gds_io_ext")
+    assert sys.modules["gdsq_test_alias.gds_io_ext"] is mod
+    del sys.modules["gdsq_test_alias.gds_io_ext"]
+
+
+def test_status_strings():
+    l = lib()
+    assert l.gdsq_status_string(0) == b"ok"
+    assert l.gdsq_status_string(2) == b"misaligned pointer"
+    assert l.gdsq_version() >= 100
+
+
+# Validation happens before any CUDA call, so these run without a GPU.
+FAKE = 0x10000  # never dereferenced
+
+
+@pytest.mark.parametrize("call,fragment", [
+    (lambda l: l.gdsq_fused_q4_0_gemv(FAKE, FAKE, FAKE, 8, 48, 1, None), b"multiple of 32"),
+    (lambda l: l.gdsq_fused_q8_0_gemv(FAKE, FAKE, FAKE, 8, 64, 0, None), b"batch 0"),
+    (lambda l: l.gdsq_fused_q8_0_gemv(FAKE, FAKE, FAKE, 8, 64, 17, None), b"batch 17"),
+    (lambda l: l.gdsq_fused_q4_0_gemv(FAKE, FAKE, FAKE, -1, 64, 1, None), b"negative"),
+    (lambda l: l.gdsq_fused_affine_q4_gemv(FAKE, FAKE, FAKE, FAKE, FAKE, 8, 100, 12, 1, None), b"multiple of 8"),
+    (lambda l: l.gdsq_fused_affine_q4_gemv(FAKE, FAKE, FAKE, FAKE, FAKE, 8, 96, 64, 1, None), b"not a multiple"),
+    (lambda l: l.gdsq_fused_q4_0_gemv(None, FAKE, FAKE, 8, 64, 1, None), b"null"),
+    (lambda l: l.gdsq_dequant_affine_q4(FAKE, FAKE, FAKE, FAKE, 100, 64, 32, None), b"whole number of rows"),
+])
+def test_invalid_arguments_are_rejected(call, fragment):
+    l = lib()
+    st = call(l)
+    assert st == 1, st
+    assert fragment in l.gdsq_last_error()
+    with pytest.raises(GdsqError):
+        check(st)
+
+
+@pytest.mark.parametrize("call", [
+    lambda l: l.gdsq_fused_q4_0_gemv(FAKE + 1, FAKE, FAKE, 8, 64, 1, None),
+    lambda l: l.gdsq_fused_q4_0_gemv(FAKE, FAKE, FAKE + 1, 8, 64, 1, None),
+    lambda l: l.gdsq_fused_affine_q4_gemv(FAKE + 2, FAKE, FAKE, FAKE, FAKE, 8, 128, 128, 1, None),
+    lambda l: l.gdsq_dequant_q4_0(FAKE + 1, FAKE, 4, None),
+    lambda l: l.gdsq_dequant_affine_q4(FAKE + 2, FAKE, FAKE, FAKE, 128, 128, 128, None),
+])
+def test_misaligned_pointers_are_rejected(call):
+    assert call(lib()) == 2
+
+
+def test_empty_work_is_a_no_op():
+    l = lib()
+    assert l.gdsq_dequant_q4_0(None, None, 0, None) == 0
+    assert l.gdsq_fused_q4_0_gemv(None, None, None, 0, 64, 1, None) == 0
