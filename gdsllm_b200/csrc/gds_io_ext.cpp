@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cerrno>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -89,10 +90,15 @@ void resolve_cufile() {
 }
 
 // gdsllm/runtime/gds_io.cu:53-69: open the driver once; failure is not fatal.
+// cuFile is used only when GDSLLM_USE_CUFILE=1 is set: opening the cuFile
+// driver can block for minutes on hosts without the nvidia-fs stack, and
+// without it cuFile's compatibility mode is the same pread + copy that the
+// fallback below performs.
 void gds_init() {
   std::lock_guard<std::mutex> lock(g_cufile_mutex);
   if (g_cufile.initialized) return;
-  resolve_cufile();
+  const char* want = getenv("GDSLLM_USE_CUFILE");
+  if (want && want[0] == '1') resolve_cufile();
   if (g_cufile.available) {
     CUfileError_t st = g_cufile.driver_open_fn();
     g_cufile.driver_open = st.err == CU_FILE_SUCCESS;
@@ -192,7 +198,7 @@ ssize_t gds_read(GdsBufferHandle& buf, const std::string& path, size_t size, off
     throw std::runtime_error("gds_read: read would exceed buffer size");
   if (size == 0) return 0;
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(buf.device_id()));
-  if (g_cufile.available && g_cufile.initialized) {
+  if (g_cufile.available && g_cufile.initialized && g_cufile.driver_open) {
     int fd = open(path.c_str(), O_RDONLY | O_DIRECT);
     if (fd < 0) fd = open(path.c_str(), O_RDONLY);
     if (fd < 0) throw std::runtime_error("gds_read: cannot open file '" + path + "': " + strerror(errno));

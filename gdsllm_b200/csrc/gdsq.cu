@@ -2,13 +2,17 @@
 //
 // One translation unit holds every kernel so that they can share the
 // device-side error word without relocatable device code.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "gdsq.h"
 #include "common.cuh"
@@ -38,6 +42,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 struct DeviceInfo {
   bool ready = false;
+  int ordinal = 0;
   int sms = 0;
   int smem_optin = 0;
 };
@@ -61,6 +66,7 @@ int device_info(const DeviceInfo** out) {
       if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
       e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
       if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem opt-in)");
+      d.ordinal = dev;
       d.ready = true;
     }
   }
@@ -89,18 +95,97 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Raises a kernel's dynamic shared memory limit once per (kernel, device).
-// The cache is one array per kernel instantiation (a function-local static of
-// this template), indexed by device.
+// Raises a kernel's dynamic shared-memory limit when a launch needs more than
+// was last set for that (kernel, device).
+std::unordered_map<const void*, int> g_smem_set[kMaxDevices];
+
 template <typename K>
 cudaError_t ensure_smem(K kernel, int bytes, int device) {
-  static int set_bytes[kMaxDevices] = {};
-  if (bytes <= 48 * 1024 || set_bytes[device] >= bytes) return cudaSuccess;
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  const void* key = reinterpret_cast<const void*>(kernel);
   std::lock_guard<std::mutex> lock(g_device_mutex);
-  if (set_bytes[device] >= bytes) return cudaSuccess;
+  auto it = g_smem_set[device].find(key);
+  if (it != g_smem_set[device].end() && it->second >= bytes) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) set_bytes[device] = bytes;
+  if (e == cudaSuccess) g_smem_set[device][key] = bytes;
   return e;
+}
+
+// ---------------------------------------------------------------------------
+// Weight tensor maps for the TMA loads of the fast GEMV.  A packed weight
+// matrix is described as a 2-D tensor of 8-byte elements: [N rows][row_bytes
+// / 8], row pitch row_bytes; one box is 32 rows x one 256-column chunk.
+// Encoded maps are cached per (pointer, shape, format, device), so repeated
+// calls on resident weights (a decode loop) pay only a hash lookup.
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q != cudaDriverEntryPointSuccess) err = cudaErrorSymbolNotFound;
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (err != cudaSuccess || !g_encode_tiled) return cuda_fail(err, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+  *out = g_encode_tiled;
+  return GDSQ_OK;
+}
+
+struct MapKey {
+  uintptr_t ptr;
+  long long row_bytes;
+  int n;
+  int fmt;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && row_bytes == o.row_bytes && n == o.n && fmt == o.fmt;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<long long>()(k.row_bytes) << 1) ^
+           ((size_t)k.n << 7) ^ ((size_t)k.fmt << 3);
+  }
+};
+std::mutex g_map_mutex;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps[kMaxDevices];
+constexpr size_t kMaxCachedMaps = 16384;
+
+template <int F>
+int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes, CUtensorMap* out) {
+  using T = GemvFormat<F>;
+  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, n, F};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    auto it = g_maps[dev.ordinal].find(key);
+    if (it != g_maps[dev.ordinal].end()) {
+      *out = it->second;
+      return GDSQ_OK;
+    }
+  }
+  PFN_cuTensorMapEncodeTiled_v12000 encode;
+  int st = get_encoder(&encode);
+  if (st != GDSQ_OK) return st;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)n};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)(T::kChunkBytes / 8), 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box,
+                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      T::kSwizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(GDSQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for a %d x %lld-byte weight", (int)r, n,
+                row_bytes);
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  if (g_maps[dev.ordinal].size() >= kMaxCachedMaps) g_maps[dev.ordinal].clear();
+  g_maps[dev.ordinal][key] = map;
+  *out = map;
+  return GDSQ_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -112,29 +197,162 @@ int batch_tile(int nb) {
   return 16;
 }
 
+// Launch plan of the fast GEMV kernel for one (format, batch tile, group, N,
+// K) on one device.
+struct GemvPlan {
+  int cs = 1;         // CTAs per cluster (K slices)
+  int stages = 1;     // ring stages per warp
+  int copy = 1;       // chunks per ring stage
+  int nclusters = 1;  // clusters launched (persistent when < row groups)
+  int smem = 0;       // dynamic shared memory bytes
+};
+
+std::mutex g_plan_mutex;
+std::unordered_map<uint64_t, GemvPlan> g_plans[kMaxDevices];
+
+// Optional override "cs:stages[:copy]" for tuning sweeps (GDSQ_GEMV_PLAN).
+bool plan_override(int* cs, int* stages, int* copy) {
+  const char* e = getenv("GDSQ_GEMV_PLAN");
+  if (!e || !*e) return false;
+  *copy = 0;
+  const int n = sscanf(e, "%d:%d:%d", cs, stages, copy);
+  return n >= 2 && *cs >= 1 && *cs <= kMaxCluster && *stages >= 1 && *stages <= kMaxStages;
+}
+
+// Picks (cs, stages, copy) by a small cost model: the busiest SM's share of
+// 256-column chunk units (plus one unit of fixed cost per CTA work item),
+// divided by an issue-efficiency factor that grows with resident warps (16
+// warps per SM are taken as enough to hide latency).  Candidates whose
+// shared memory does not fit are skipped.
 template <int F, int B, int GS>
-int launch_fast(const GemvParams& p, const DeviceInfo& dev, cudaStream_t stream, int device) {
-  const GemvSmemLayout L = gemv_smem_layout<F>(B, p.K, GS);
+int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
+  using T = GemvFormat<F>;
   auto kernel = gemv_fast_kernel<F, B, GS>;
-  cudaError_t e = ensure_smem(kernel, L.total, device);
+  const int R = (N + 31) / 32;
+  const int C = K / kChunkCols;
+  int force_cs = 0, force_st = 0, force_cp = 0;
+  const bool forced = plan_override(&force_cs, &force_st, &force_cp);
+  double best = 1e30;
+  bool found = false;
+  for (int cs = 1; cs <= kMaxCluster; cs *= 2) {
+    if (cs > C) break;
+    if (forced && cs != force_cs) continue;
+    const int cslice = (C + cs - 1) / cs;
+    const int mw = (cslice + kGemvWarps - 1) / kGemvWarps;
+    for (int cp = 1; cp <= T::kMaxCopyChunks; ++cp) {
+      if (forced && force_cp && cp != force_cp) continue;
+      const int nsteps = (mw + cp - 1) / cp;
+      for (int st = 1; st <= 4; ++st) {
+        if (forced && st != force_st) continue;
+        if (!forced && st > 1 && st > nsteps * ((R + 147) / 148)) break;
+        const GemvSmemLayout L = gemv_smem_layout<F>(B, K, GS, cs, st, cp);
+        if (L.total > dev.smem_optin) continue;
+        cudaError_t e = ensure_smem(kernel, L.total, dev.ordinal);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
+        int occ = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, L.total);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (occ < 1) continue;
+        const long long slots = (long long)dev.sms * occ;
+        const long long ctas = (long long)R * cs;
+        double load;
+        long long resident;
+        int nclusters;
+        if (ctas <= slots) {
+          nclusters = R;
+          resident = (ctas + dev.sms - 1) / dev.sms;
+          load = (double)resident * (cslice + 1);
+        } else {
+          nclusters = (int)(slots / cs);
+          const int items = (R + nclusters - 1) / nclusters;
+          resident = occ;
+          load = (double)occ * items * (cslice + 1);
+        }
+        const double warps = (double)resident * kGemvWarps;
+        const double eff = warps >= 16 ? 1.0 : warps / 16.0;
+        const double cost = load / eff * (1.0 + 0.02 * cs) / (1.0 + 0.01 * st) * (1.0 + 0.005 * cp);
+        if (cost < best) {
+          best = cost;
+          found = true;
+          out->cs = cs;
+          out->stages = st;
+          out->copy = cp;
+          out->nclusters = nclusters;
+          out->smem = L.total;
+        }
+      }
+    }
+  }
+  if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no GEMV launch plan fits shared memory");
+  return GDSQ_OK;
+}
+
+template <int F, int B, int GS>
+int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
+  const uint64_t key = ((uint64_t)F << 60) | ((uint64_t)B << 54) | ((uint64_t)GS << 44) |
+                       ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
+  GemvPlan plan;
+  bool have = false;
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = g_plans[dev.ordinal].find(key);
+    if (it != g_plans[dev.ordinal].end()) {
+      plan = it->second;
+      have = true;
+    }
+  }
+  if (!have) {
+    int st = make_plan<F, B, GS>(p.N, p.K, dev, &plan);
+    if (st != GDSQ_OK) return st;
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    g_plans[dev.ordinal][key] = plan;
+  }
+  CUtensorMap wmap;
+  int mst = weight_map<F>(dev, p.w, p.N, p.row_bytes, &wmap);
+  if (mst != GDSQ_OK) return mst;
+  auto kernel = gemv_fast_kernel<F, B, GS>;
+  cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
-  const dim3 grid((p.N + 31) / 32);
-  e = launch(kernel, grid, dim3(kGemvWarps * 32), L.total, stream, g_pdl_enabled != 0, p);
+  p.cs = plan.cs;
+  p.stages = plan.stages;
+  p.copy = plan.copy;
+  p.num_rg = (p.N + 31) / 32;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.nclusters * plan.cs);
+  cfg.blockDim = dim3(kGemvWarps * 32);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (plan.cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = plan.cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g_pdl_enabled) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
   if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-  (void)dev;
   return GDSQ_OK;
 }
 
 template <int F, int GS>
-int launch_fast_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t stream,
-                      int device) {
+int launch_fast_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t stream) {
   switch (batch_tile(p.nb)) {
-    case 1: return launch_fast<F, 1, GS>(p, dev, stream, device);
-    case 2: return launch_fast<F, 2, GS>(p, dev, stream, device);
-    case 3: return launch_fast<F, 3, GS>(p, dev, stream, device);
-    case 4: return launch_fast<F, 4, GS>(p, dev, stream, device);
-    case 8: return launch_fast<F, 8, GS>(p, dev, stream, device);
-    default: return launch_fast<F, 16, GS>(p, dev, stream, device);
+    case 1: return launch_fast<F, 1, GS>(p, dev, stream);
+    case 2: return launch_fast<F, 2, GS>(p, dev, stream);
+    case 3: return launch_fast<F, 3, GS>(p, dev, stream);
+    case 4: return launch_fast<F, 4, GS>(p, dev, stream);
+    case 8: return launch_fast<F, 8, GS>(p, dev, stream);
+    default: return launch_fast<F, 16, GS>(p, dev, stream);
   }
 }
 
@@ -146,9 +364,14 @@ int launch_generic(const GemvParams& p, cudaStream_t stream) {
   return GDSQ_OK;
 }
 
+// Smallest shared-memory footprint of the fast kernel (stages = 1, widest
+// cluster split): if even this does not fit, use the generic kernel.
 template <int F>
-int fast_smem_bytes(int nb, int K, int group) {
-  return gemv_smem_layout<F>(batch_tile(nb), K, group).total;
+int fast_min_smem(int nb, int K, int group) {
+  const int C = K / kChunkCols;
+  int cs = 1;
+  while (cs * 2 <= kMaxCluster && cs * 2 <= C) cs *= 2;
+  return gemv_smem_layout<F>(batch_tile(nb), K, group, cs, 1, 1).total;
 }
 
 int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases, const void* x,
@@ -193,10 +416,8 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
   const DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
   if (st != GDSQ_OK) return st;
-  int device = 0;
-  cudaGetDevice(&device);
 
-  GemvParams p;
+  GemvParams p = {};
   p.w = static_cast<const uint8_t*>(w);
   p.scales = static_cast<const __half*>(scales);
   p.biases = static_cast<const __half*>(biases);
@@ -212,23 +433,22 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
 
   const bool shape_ok = in_dim % kChunkCols == 0 && aligned(w, 16) && aligned(x, 16);
   if (fmt == kFmtQ4_0) {
-    if (shape_ok && fast_smem_bytes<kFmtQ4_0>(batch, in_dim, 0) <= dev->smem_optin)
-      return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream, device);
+    if (shape_ok && fast_min_smem<kFmtQ4_0>(batch, in_dim, 0) <= dev->smem_optin)
+      return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream);
     return launch_generic<kFmtQ4_0>(p, stream);
   }
   if (fmt == kFmtQ8_0) {
-    if (shape_ok && fast_smem_bytes<kFmtQ8_0>(batch, in_dim, 0) <= dev->smem_optin)
-      return launch_fast_batch<kFmtQ8_0, 0>(p, *dev, stream, device);
+    if (shape_ok && fast_min_smem<kFmtQ8_0>(batch, in_dim, 0) <= dev->smem_optin)
+      return launch_fast_batch<kFmtQ8_0, 0>(p, *dev, stream);
     return launch_generic<kFmtQ8_0>(p, stream);
   }
   const bool group_ok = group == 32 || group == 64 || group == 128 || group == 256;
-  if (shape_ok && group_ok &&
-      fast_smem_bytes<kFmtAffineQ4>(batch, in_dim, group) <= dev->smem_optin) {
+  if (shape_ok && group_ok && fast_min_smem<kFmtAffineQ4>(batch, in_dim, group) <= dev->smem_optin) {
     switch (group) {
-      case 32: return launch_fast_batch<kFmtAffineQ4, 32>(p, *dev, stream, device);
-      case 64: return launch_fast_batch<kFmtAffineQ4, 64>(p, *dev, stream, device);
-      case 128: return launch_fast_batch<kFmtAffineQ4, 128>(p, *dev, stream, device);
-      default: return launch_fast_batch<kFmtAffineQ4, 256>(p, *dev, stream, device);
+      case 32: return launch_fast_batch<kFmtAffineQ4, 32>(p, *dev, stream);
+      case 64: return launch_fast_batch<kFmtAffineQ4, 64>(p, *dev, stream);
+      case 128: return launch_fast_batch<kFmtAffineQ4, 128>(p, *dev, stream);
+      default: return launch_fast_batch<kFmtAffineQ4, 256>(p, *dev, stream);
     }
   }
   return launch_generic<kFmtAffineQ4>(p, stream);

@@ -7,24 +7,28 @@
 //   kernel_fused_affine_q4_gemv  gdsllm/runtime/affine_q4_dequant.cu:79-158
 //
 // Fast path (weights 16-byte aligned, K % 256 == 0):
-//   * A CTA owns 32 consecutive output rows and 4 warps.  Lane l of every
-//     warp works on row (row0 + l); the warps split the row's 256-column
-//     "chunks" round-robin.
+//   * Work item = 32 consecutive output rows ("row group").  Lane l of every
+//     warp computes row (row0 + l).
+//   * K is split across a thread-block cluster of `cs` CTAs: CTA rank r owns
+//     256-column chunks [C*r/cs, C*(r+1)/cs).  Inside a CTA, each of the 4
+//     warps owns a contiguous run of those chunks.
 //   * Each warp streams its chunks through a private ring of shared-memory
-//     stages.  A stage holds one chunk of all 32 rows; every lane issues one
-//     1-D bulk copy (cp.async.bulk) of its own row's chunk bytes, and lane 0
-//     arms the stage's mbarrier with the stage's byte count.  No register or
-//     LSU work is spent moving weights.
-//   * The activations are copied once per CTA into shared memory, permuted so
-//     that the pair order matches the order in which the dequantizer produces
-//     weight pairs.  All 32 lanes then read the same activation address, so
-//     each 16-byte shared load is a broadcast.
+//     stages.  A stage holds 1 or 2 chunks (plan) of all 32 rows, each
+//     chunk one 2-D TMA box (32 rows x chunk bytes) of the weight matrix's
+//     tensor map, issued by lane 0, which also arms the stage's mbarrier.
+//     Rows past N arrive as zeros.  Copies for the next stages are in flight
+//     while the current one is computed, and the ring keeps streaming across
+//     row groups when a cluster owns several.
+//   * The activations of the CTA's K slice are staged once in shared memory,
+//     permuted so that pair order matches the dequantizer's output order; all
+//     32 lanes read the same address, so activation loads are broadcasts.
 //   * Nibbles become exact fp16 (q - 8) with the magic-number trick; products
 //     are summed in fp16 pairs over at most 16 terms per 32-column block and
-//     then in fp32 across blocks.  Q8_0 is dequantized straight to fp32 and
-//     summed in fp32.
-//   * Partial sums of the 4 warps meet in shared memory; one fp16 store per
-//     (batch row, output row).
+//     then in fp32.  Q8_0 is dequantized straight to fp32 and summed in fp32.
+//   * Per row group: warps meet in shared memory; with cs > 1 every CTA writes
+//     its partial sums into the cluster leader's shared memory (distributed
+//     shared memory), and after a cluster barrier the leader adds the cs
+//     partials in rank order and stores fp16 y.
 //
 // Generic path: any K % 32 == 0 (group_size % 8 == 0 for affine) and 2-byte
 // (4-byte for affine words) alignment; one warp per row, plain loads.
@@ -38,33 +42,46 @@ enum WeightFormat : int { kFmtQ4_0 = 0, kFmtQ8_0 = 1, kFmtAffineQ4 = 2 };
 
 constexpr int kGemvWarps = 4;
 constexpr int kChunkCols = 256;
+constexpr int kMaxStages = 8;
+constexpr int kMaxCluster = 8;
 
 template <int F>
 struct GemvFormat;
 
+// One chunk of 32 rows lands in shared memory as a dense [32][kChunkBytes]
+// box.  For Q4_0 and Q8_0 the row pitch is 36 or 68 words (= 4 mod 32), so
+// 16-byte loads of 8 consecutive lanes hit 8 distinct bank groups.  The
+// affine pitch is 128 bytes, so its boxes use the 128-byte swizzle (16-byte
+// unit u of row r is stored at unit u ^ (r % 8)).
 template <>
 struct GemvFormat<kFmtQ4_0> {
   static constexpr int kChunkBytes = 144;  // 8 blocks x 18 B
-  static constexpr int kSlotStride = 144;  // 36 words = 4 (mod 32): LDS.128 conflict-free
-  static constexpr int kStages = 4;
+  static constexpr int kMaxCopyChunks = 2;  // chunks (TMA boxes) per ring stage, at most
+  static constexpr bool kSwizzle = false;
   static constexpr int kXBytes = 2;        // activations kept as permuted fp16
 };
 
 template <>
 struct GemvFormat<kFmtQ8_0> {
   static constexpr int kChunkBytes = 272;  // 8 blocks x 34 B
-  static constexpr int kSlotStride = 272;  // 68 words = 4 (mod 32)
-  static constexpr int kStages = 2;
+  static constexpr int kMaxCopyChunks = 1;
+  static constexpr bool kSwizzle = false;
   static constexpr int kXBytes = 4;        // activations kept as fp32
 };
 
 template <>
 struct GemvFormat<kFmtAffineQ4> {
   static constexpr int kChunkBytes = 128;  // 32 words of 8 nibbles
-  static constexpr int kSlotStride = 144;  // padded from 128 B to avoid bank conflicts
-  static constexpr int kStages = 4;
+  static constexpr int kMaxCopyChunks = 2;
+  static constexpr bool kSwizzle = true;
   static constexpr int kXBytes = 2;
 };
+
+// Bytes of one ring stage holding `copy` chunks of 32 rows.
+template <int F>
+__host__ __device__ constexpr int stage_bytes(int copy) {
+  return copy * 32 * GemvFormat<F>::kChunkBytes;
+}
 
 struct GemvParams {
   const uint8_t* w;       // packed weights, row-major
@@ -77,63 +94,76 @@ struct GemvParams {
   int nb;                 // batch rows actually present (<= template B)
   int group;              // affine group size
   long long row_bytes;    // packed bytes per weight row
+  int cs;                 // CTAs per cluster (K slices)
+  int stages;             // ring stages per warp (1..kMaxStages)
+  int copy;               // chunks per ring stage (1..kMaxCopyChunks)
+  int num_rg;             // row groups = ceil(N / 32)
 };
 
 // Shared-memory carve-up of the fast kernel, identical on host and device.
 struct GemvSmemLayout {
-  int ring;   // byte offsets from the dynamic smem base
+  int ring;       // byte offsets from the dynamic smem base
   int xs;
   int xsum;
   int sb;
   int sb_stride;  // words per row of the (scale, bias) table
   int red;
+  int slots;
   int total;
+  int kslice;     // columns of the largest K slice
 };
 
 template <int F>
-__host__ __device__ inline GemvSmemLayout gemv_smem_layout(int B, int K, int group) {
+__host__ __device__ inline GemvSmemLayout gemv_smem_layout(int B, int K, int group, int cs,
+                                                           int stages, int copy) {
   using T = GemvFormat<F>;
   GemvSmemLayout L;
-  int off = 128;  // mbarriers: kGemvWarps * kStages * 8 <= 128 bytes
+  const int C = K / kChunkCols;
+  (void)sizeof(T);
+  L.kslice = (C + cs - 1) / cs * kChunkCols;
+  int off = 1024;  // mbarriers (kGemvWarps * kMaxStages * 8 bytes); ring 1024-aligned
   L.ring = off;
-  off += kGemvWarps * T::kStages * 32 * T::kSlotStride;
+  off += kGemvWarps * stages * stage_bytes<F>(copy);
   L.xs = off;
-  off += B * K * T::kXBytes;
+  off += B * L.kslice * T::kXBytes;
   L.xsum = off;
   L.sb = off;
   L.sb_stride = 0;
   if (F == kFmtAffineQ4) {
-    const int G = K / group;
-    off += B * G * 4;
+    const int gs = L.kslice / group;
+    off += B * gs * 4;
     L.sb = off;
-    L.sb_stride = G | 1;  // odd word stride: conflict-free per-lane reads
+    L.sb_stride = gs | 1;  // odd word stride: conflict-free per-lane reads
     off += 32 * L.sb_stride * 4;
   }
   L.red = off;
-  off += kGemvWarps * B * 32 * 4;
-  L.total = off;
+  off += 2 * kGemvWarps * B * 32 * 4;
+  L.slots = off;
+  if (cs > 1) off += 2 * cs * B * 32 * 4;
+  L.total = off + 1024;  // slack to align the base to 1024 bytes at run time
   return L;
 }
 
 // ---------------------------------------------------------------------------
-// Activation staging (runs after the programmatic-dependency wait).
+// Activation staging: columns [col0, col0 + ncols) of x into shared memory,
+// row stride ncols_max.  Runs after the programmatic-dependency wait.
 
 // Q4_0: per 32-column block, 16 half2 in the order the dequantizer emits:
 // for qs word i (bytes 4i..4i+3):
 //   (x[4i], x[4i+2]), (x[16+4i], x[18+4i]), (x[4i+1], x[4i+3]), (x[17+4i], x[19+4i])
 __device__ __forceinline__ void stage_x_q4_0(const __half* __restrict__ x, uint8_t* xs, int nb,
-                                             int B, int K) {
-  const int nblk = K / 32;
+                                             int B, int K, int col0, int ncols, int ld) {
+  const int nblk = ncols / 32;
   for (int u = threadIdx.x; u < B * nblk; u += blockDim.x) {
     const int b = u / nblk;
     const int blk = u - b * nblk;
-    uint4* dst = reinterpret_cast<uint4*>(xs) + (size_t)u * 4;
+    uint4* dst = reinterpret_cast<uint4*>(xs + ((size_t)b * ld + blk * 32) * 2);
     if (b >= nb) {
       const uint4 z = make_uint4(0, 0, 0, 0);
       dst[0] = z; dst[1] = z; dst[2] = z; dst[3] = z;
       continue;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)b * K + blk * 32);
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + blk * 32);
     uint32_t h[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -154,17 +184,18 @@ __device__ __forceinline__ void stage_x_q4_0(const __half* __restrict__ x, uint8
 
 // Q8_0: plain fp32 copy of x.
 __device__ __forceinline__ void stage_x_f32(const __half* __restrict__ x, uint8_t* xs, int nb,
-                                            int B, int K) {
-  const int n8 = K / 8;
+                                            int B, int K, int col0, int ncols, int ld) {
+  const int n8 = ncols / 8;
   for (int u = threadIdx.x; u < B * n8; u += blockDim.x) {
     const int b = u / n8;
-    float4* dst = reinterpret_cast<float4*>(xs) + (size_t)u * 2;
+    const int j = u - b * n8;
+    float4* dst = reinterpret_cast<float4*>(xs + ((size_t)b * ld + j * 8) * 4);
     if (b >= nb) {
       dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
       dst[1] = dst[0];
       continue;
     }
-    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)u * 8);
+    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
     const float2 a = __half22float2(u32_as_h2(v.x));
     const float2 c = __half22float2(u32_as_h2(v.y));
     const float2 e = __half22float2(u32_as_h2(v.z));
@@ -175,21 +206,25 @@ __device__ __forceinline__ void stage_x_f32(const __half* __restrict__ x, uint8_
 }
 
 // Affine: per 8-column word, (x0,x4),(x1,x5),(x2,x6),(x3,x7); plus the fp32
-// sum of x over each quantization group (needed for the bias term).
+// sum of x over each quantization group (needed for the bias term), stored
+// at xsum[b * (ld / GS) + group].
 template <int GS>
 __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uint8_t* xs,
-                                               float* xsum, int nb, int B, int K) {
+                                               float* xsum, int nb, int B, int K, int col0,
+                                               int ncols, int ld) {
   constexpr int kLanesPerGroup = GS / 8;  // 4..32, divides 32
-  const int n8 = K / 8;
+  const int n8 = ncols / 8;
   const int total = B * n8;
   for (int base = threadIdx.x & ~31; base < total; base += blockDim.x) {
     const int u = base + (threadIdx.x & 31);
     float s = 0.f;
+    int b = 0, j = 0;
     if (u < total) {
-      const int b = u / n8;
+      b = u / n8;
+      j = u - b * n8;
       uint4 o = make_uint4(0, 0, 0, 0);
       if (b < nb) {
-        const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)u * 8);
+        const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
         o.x = __byte_perm(v.x, v.z, 0x5410);  // x0, x4
         o.y = __byte_perm(v.x, v.z, 0x7632);  // x1, x5
         o.z = __byte_perm(v.y, v.w, 0x5410);  // x2, x6
@@ -200,28 +235,29 @@ __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uin
         const float2 g = __half22float2(u32_as_h2(v.w));
         s = ((a.x + a.y) + (c.x + c.y)) + ((e.x + e.y) + (g.x + g.y));
       }
-      reinterpret_cast<uint4*>(xs)[u] = o;
+      *reinterpret_cast<uint4*>(xs + ((size_t)b * ld + j * 8) * 2) = o;
     }
 #pragma unroll
     for (int m = 1; m < kLanesPerGroup; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-    if (u < total && (u % kLanesPerGroup) == 0) xsum[u / kLanesPerGroup] = s;
+    if (u < total && (j % kLanesPerGroup) == 0) xsum[b * (ld / GS) + j / kLanesPerGroup] = s;
   }
 }
 
 // ---------------------------------------------------------------------------
-// Per-chunk compute: one lane, one row, 256 columns.
+// Per-chunk compute: one lane, one row, 256 columns.  `src` is the shared
+// address of this lane's chunk bytes, `xa` the shared address of the staged
+// activations of this chunk for batch row 0 and `xb` the byte distance
+// between batch rows.
 
 template <int B>
-__device__ __forceinline__ void chunk_q4_0(const uint8_t* slot, const uint8_t* xs, int K, int c,
+__device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t xb,
                                            float (&acc)[B]) {
   uint32_t w[36];
-  const uint4* s4 = reinterpret_cast<const uint4*>(slot);
 #pragma unroll
   for (int j = 0; j < 9; ++j) {
-    const uint4 v = s4[j];
+    const uint4 v = lds128(src + 16 * j);
     w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
   }
-  const uint4* xc = reinterpret_cast<const uint4*>(xs) + (size_t)c * (kChunkCols / 8);
 #pragma unroll
   for (int blk = 0; blk < 8; ++blk) {
     const int o = 18 * blk;  // byte offset of the block inside the chunk
@@ -243,92 +279,93 @@ __device__ __forceinline__ void chunk_q4_0(const uint8_t* slot, const uint8_t* x
     for (int i = 0; i < 4; ++i) unpack_nibbles_minus8(q[i], &wv[4 * i]);
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      const uint4* xr = xc + (size_t)b * (K / 8) + blk * 4;
-      __half2 a0 = u32_as_h2(0u), a1 = u32_as_h2(0u);
+      // four independent fp16 chains of 4 products each
+      __half2 a[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint4 xv = xr[i];
-        a0 = __hfma2(wv[4 * i + 0], u32_as_h2(xv.x), a0);
-        a1 = __hfma2(wv[4 * i + 1], u32_as_h2(xv.y), a1);
-        a0 = __hfma2(wv[4 * i + 2], u32_as_h2(xv.z), a0);
-        a1 = __hfma2(wv[4 * i + 3], u32_as_h2(xv.w), a1);
+        const uint4 xv = lds128(xa + b * xb + (blk * 4 + i) * 16);
+        a[i] = __hmul2(wv[4 * i + 0], u32_as_h2(xv.x));
+        a[i] = __hfma2(wv[4 * i + 1], u32_as_h2(xv.y), a[i]);
+        a[i] = __hfma2(wv[4 * i + 2], u32_as_h2(xv.z), a[i]);
+        a[i] = __hfma2(wv[4 * i + 3], u32_as_h2(xv.w), a[i]);
       }
-      const float2 f = __half22float2(__hadd2(a0, a1));
+      const float2 f = __half22float2(__hadd2(__hadd2(a[0], a[1]), __hadd2(a[2], a[3])));
       acc[b] = fmaf(d, f.x + f.y, acc[b]);
     }
   }
 }
 
 template <int B>
-__device__ __forceinline__ void chunk_q8_0(const uint8_t* slot, const uint8_t* xs, int K, int c,
+__device__ __forceinline__ void chunk_q8_0(uint32_t src, uint32_t xa, uint32_t xb,
                                            float (&acc)[B]) {
-  uint32_t w[68];
-  const uint4* s4 = reinterpret_cast<const uint4*>(slot);
-#pragma unroll
-  for (int j = 0; j < 17; ++j) {
-    const uint4 v = s4[j];
-    w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
-  }
-  const float4* xc = reinterpret_cast<const float4*>(xs) + (size_t)c * (kChunkCols / 4);
   constexpr float kBias = 8388736.0f;  // 2^23 + 128
+  // Two blocks (68 bytes) at a time: words [17*pr, 17*pr + 17) of the chunk.
 #pragma unroll
-  for (int blk = 0; blk < 8; ++blk) {
-    const int o = 34 * blk;
-    uint32_t d16, q[8];
-    if ((blk & 1) == 0) {
-      const int wi = o / 4;
-      d16 = w[wi] & 0xFFFFu;
+  for (int pr = 0; pr < 4; ++pr) {
+    uint32_t w[20];
+    const int w0 = 17 * pr;       // first word of the pair
+    const int u0 = w0 / 4;        // first 16-byte unit covering it
 #pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[wi + i], w[wi + i + 1], 16);
-    } else {
-      const int wi = (o - 2) / 4;
-      d16 = w[wi] >> 16;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = w[wi + 1 + i];
+    for (int u = 0; u < 5; ++u) {
+      const uint4 v = lds128(src + 16 * (u0 + u));
+      w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
     }
-    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(d16)));
-    float wf[32];
+    const int sh = w0 - 4 * u0;  // 0..3
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t u = q[i] ^ 0x80808080u;  // int8 -> excess-128
+    for (int half = 0; half < 2; ++half) {
+      const int blk = 2 * pr + half;
+      uint32_t d16, q[8];
+      if (half == 0) {
+        d16 = w[sh] & 0xFFFFu;
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        wf[4 * i + k] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + k)) - kBias;
-    }
+        for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[sh + i], w[sh + i + 1], 16);
+      } else {
+        d16 = w[sh + 8] >> 16;
 #pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const float4* xr = xc + (size_t)b * (K / 4) + blk * 8;
-      float s0 = 0.f, s1 = 0.f;
+        for (int i = 0; i < 8; ++i) q[i] = w[sh + 9 + i];
+      }
+      const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(d16)));
+      float wf[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 xv = xr[i];
-        s0 = fmaf(wf[4 * i + 0], xv.x, s0);
-        s1 = fmaf(wf[4 * i + 1], xv.y, s1);
-        s0 = fmaf(wf[4 * i + 2], xv.z, s0);
-        s1 = fmaf(wf[4 * i + 3], xv.w, s1);
+        const uint32_t u = q[i] ^ 0x80808080u;  // int8 -> excess-128
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          wf[4 * i + k] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + k)) - kBias;
       }
-      acc[b] = fmaf(d, s0 + s1, acc[b]);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 xv = lds128f(xa + b * xb + (blk * 8 + i) * 16);
+          s[i & 3] = fmaf(wf[4 * i + 0], xv.x, s[i & 3]);
+          s[i & 3] = fmaf(wf[4 * i + 1], xv.y, s[i & 3]);
+          s[i & 3] = fmaf(wf[4 * i + 2], xv.z, s[i & 3]);
+          s[i & 3] = fmaf(wf[4 * i + 3], xv.w, s[i & 3]);
+        }
+        acc[b] = fmaf(d, (s[0] + s[1]) + (s[2] + s[3]), acc[b]);
+      }
     }
   }
 }
 
 // Affine: sum_k (n_k*s + b) x_k = s * sum_k (n_k - 8) x_k + (b + 8 s) * sum_k x_k
 // over each group; the (n - 8) form keeps the fp16 partial sums small.
+// `sb_row` (shared address of this lane's (scale, bias) row) and `xsum` are
+// indexed by the group's position in the K slice, starting at g0.
 template <int B, int GS>
-__device__ __forceinline__ void chunk_affine(const uint8_t* slot, const uint8_t* xs,
-                                             const float* xsum, const uint32_t* sb_row, int K,
-                                             int c, float (&acc)[B]) {
+__device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_t xa, uint32_t xb,
+                                             uint32_t xsum, uint32_t xsum_b, uint32_t sb_row,
+                                             int g0, float (&acc)[B]) {
   uint32_t w[32];
-  const uint4* s4 = reinterpret_cast<const uint4*>(slot);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint4 v = s4[j];
+    const uint4 v = lds128(src + 16 * (j ^ swz));  // 128-byte swizzled box row
     w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
   }
   constexpr int kGroupsPerChunk = kChunkCols / GS;
   constexpr int kWordsPerGroup = GS / 8;
-  const uint4* xc = reinterpret_cast<const uint4*>(xs) + (size_t)c * (kChunkCols / 8);
-  const int G = K / GS;
 #pragma unroll
   for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
     float P[B];
@@ -341,141 +378,262 @@ __device__ __forceinline__ void chunk_affine(const uint8_t* slot, const uint8_t*
       for (int t = 0; t < 4; ++t) unpack_nibbles_minus8(w[gi * kWordsPerGroup + sub * 4 + t], &wv[4 * t]);
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        const uint4* xr = xc + (size_t)b * (K / 8) + gi * kWordsPerGroup + sub * 4;
-        __half2 a0 = u32_as_h2(0u), a1 = u32_as_h2(0u);
+        __half2 a[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const uint4 xv = xr[t];
-          a0 = __hfma2(wv[4 * t + 0], u32_as_h2(xv.x), a0);
-          a1 = __hfma2(wv[4 * t + 1], u32_as_h2(xv.y), a1);
-          a0 = __hfma2(wv[4 * t + 2], u32_as_h2(xv.z), a0);
-          a1 = __hfma2(wv[4 * t + 3], u32_as_h2(xv.w), a1);
+          const uint4 xv = lds128(xa + b * xb + (gi * kWordsPerGroup + sub * 4 + t) * 16);
+          a[t] = __hmul2(wv[4 * t + 0], u32_as_h2(xv.x));
+          a[t] = __hfma2(wv[4 * t + 1], u32_as_h2(xv.y), a[t]);
+          a[t] = __hfma2(wv[4 * t + 2], u32_as_h2(xv.z), a[t]);
+          a[t] = __hfma2(wv[4 * t + 3], u32_as_h2(xv.w), a[t]);
         }
-        const float2 f = __half22float2(__hadd2(a0, a1));
+        const float2 f = __half22float2(__hadd2(__hadd2(a[0], a[1]), __hadd2(a[2], a[3])));
         P[b] += f.x + f.y;
       }
     }
-    const int g = c * kGroupsPerChunk + gi;
-    const float2 sbf = __half22float2(u32_as_h2(sb_row[g]));
+    const int g = g0 + gi;
+    const float2 sbf = __half22float2(u32_as_h2(lds32(sb_row + 4 * g)));
     const float s = sbf.x;
     const float b8 = fmaf(8.f, s, sbf.y);
 #pragma unroll
-    for (int b = 0; b < B; ++b) acc[b] = fmaf(s, P[b], fmaf(b8, xsum[b * G + g], acc[b]));
+    for (int b = 0; b < B; ++b)
+      acc[b] = fmaf(s, P[b], fmaf(b8, lds32f(xsum + b * xsum_b + 4 * g), acc[b]));
   }
+}
+
+// ---------------------------------------------------------------------------
+// Cluster helpers (distributed shared memory).
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address of `local` (a shared::cta address in this CTA's window) in the
+// shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(const void* local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(local)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // ---------------------------------------------------------------------------
 
 template <int F, int B, int GS>
 __global__ void __launch_bounds__(kGemvWarps * 32)
-    gemv_fast_kernel(const GemvParams p) {
+    gemv_fast_kernel(const GemvParams p, const __grid_constant__ CUtensorMap wmap) {
   using T = GemvFormat<F>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const GemvSmemLayout L = gemv_smem_layout<F>(B, p.K, GS);
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // TMA destinations (the 128-byte swizzle in particular) need a 1024-byte
+  // aligned base; the layout reserves the slack.
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  const int cs = p.cs;
+  const int S = p.stages;
+  const int CP = p.copy;
+  const GemvSmemLayout L = gemv_smem_layout<F>(B, p.K, GS, cs, S, CP);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int K = p.K;
-  const int nchunks = K / kChunkCols;
+  const int C = K / kChunkCols;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * T::kStages;
-  uint8_t* ring = smem + L.ring + warp * (T::kStages * 32 * T::kSlotStride);
+  const int crank = cs > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int cluster = blockIdx.x / cs;
+  const int nclusters = gridDim.x / cs;
+  const int nitems = cluster < p.num_rg ? (p.num_rg - 1 - cluster) / nclusters + 1 : 0;
+
+  // This CTA's K slice and this warp's contiguous chunks inside it.
+  const int c0 = (C * crank) / cs;
+  const int cslice = (C * (crank + 1)) / cs - c0;
+  const int per_warp = (cslice + kGemvWarps - 1) / kGemvWarps;
+  const int wc0 = min(cslice, warp * per_warp);            // slice-local
+  const int mw = min(cslice, wc0 + per_warp) - wc0;        // chunks per item
+  const int nsteps = (mw + CP - 1) / CP;
+  const int total = nitems * nsteps;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
+  uint8_t* ring = smem + L.ring + warp * (S * stage_bytes<F>(CP));
   uint8_t* xs = smem + L.xs;
   float* xsum = reinterpret_cast<float*>(smem + L.xsum);
   uint32_t* sb = reinterpret_cast<uint32_t*>(smem + L.sb);
   float* red = reinterpret_cast<float*>(smem + L.red);
-
-  const int row0 = blockIdx.x * 32;
-  const int nvalid = min(32, p.N - row0);
-  const bool valid = lane < nvalid;
-  const uint8_t* wrow = p.w + (size_t)(row0 + (valid ? lane : 0)) * p.row_bytes;
-  const uint32_t stage_bytes = static_cast<uint32_t>(nvalid * T::kChunkBytes);
-  const int nmine = warp < nchunks ? (nchunks - warp + kGemvWarps - 1) / kGemvWarps : 0;
+  float* slots = reinterpret_cast<float*>(smem + L.slots);
+  const uint32_t ring_a = smem_addr(ring) + lane * T::kChunkBytes;  // this lane's row, stage 0, chunk 0
   const uint64_t policy = l2_policy_evict_first();
 
   if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < T::kStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
+    if (warp == 0) prefetch_tensor_map(&wmap);
   }
   __syncwarp();
 
-  auto issue = [&](int stage, int chunk) {
-    if (lane == 0) mbar_arrive_expect_tx(&bars[stage], stage_bytes);
-    __syncwarp();
-    if (valid)
-      bulk_copy_g2s_hint(ring + stage * (32 * T::kSlotStride) + lane * T::kSlotStride,
-                         wrow + (size_t)chunk * T::kChunkBytes, T::kChunkBytes, &bars[stage],
-                         policy);
+  // Producer cursor: the next (item, step) to copy and the stage it goes to.
+  int p_item = 0, p_step = 0, p_stage = 0, issued = 0;
+  auto issue_next = [&]() {
+    if (lane == 0) {
+      const int row0 = (cluster + p_item * nclusters) * 32;
+      const int chunk = c0 + wc0 + p_step * CP;
+      const int nch = min(CP, mw - p_step * CP);
+      uint8_t* dst = ring + p_stage * stage_bytes<F>(CP);
+      mbar_arrive_expect_tx(&bars[p_stage], static_cast<uint32_t>(nch * 32 * T::kChunkBytes));
+      for (int j = 0; j < nch; ++j)
+        tma_load_2d(dst + j * (32 * T::kChunkBytes), &wmap, (chunk + j) * (T::kChunkBytes / 8), row0,
+                    &bars[p_stage], policy);
+    }
+    ++issued;
+    if (++p_step == nsteps) { p_step = 0; ++p_item; }
+    if (++p_stage == S) p_stage = 0;
   };
 
   // Weights do not depend on the previous kernel: start streaming them now.
-  const int npro = min(T::kStages, nmine);
-  for (int i = 0; i < npro; ++i) issue(i, warp + i * kGemvWarps);
+  const int npro = min(S, total);
+  for (int t = 0; t < npro; ++t) issue_next();
   pdl_launch_dependents();
 
-  if constexpr (F == kFmtAffineQ4) {
-    const int G = K / GS;
-    for (int idx = threadIdx.x; idx < 32 * G; idx += blockDim.x) {
-      const int r = idx / G;
-      const int g = idx - r * G;
-      uint32_t v = 0;
-      if (r < nvalid) {
-        const size_t gi = (size_t)(row0 + r) * G + g;
-        const uint32_t s = __half_as_ushort(p.scales[gi]);
-        const uint32_t b = __half_as_ushort(p.biases[gi]);
-        v = s | (b << 16);
+  const int gslice = F == kFmtAffineQ4 ? cslice * kChunkCols / GS : 0;
+  auto load_sb = [&](int row0) {
+    if constexpr (F == kFmtAffineQ4) {
+      const int G = K / GS;
+      const int nvalid = min(32, p.N - row0);
+      for (int idx = threadIdx.x; idx < 32 * gslice; idx += blockDim.x) {
+        const int r = idx / gslice;
+        const int g = idx - r * gslice;
+        uint32_t v = 0;
+        if (r < nvalid) {
+          const size_t gi = (size_t)(row0 + r) * G + c0 * (kChunkCols / GS) + g;
+          v = (uint32_t)__half_as_ushort(p.scales[gi]) | ((uint32_t)__half_as_ushort(p.biases[gi]) << 16);
+        }
+        sb[r * L.sb_stride + g] = v;
       }
-      sb[r * L.sb_stride + g] = v;
     }
-  }
+  };
+  if (nitems > 0) load_sb(cluster * 32);
 
   pdl_wait_primary();  // activations are produced by the previous kernel
-  if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K);
-  else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K);
-  else stage_x_affine<GS>(p.x, xs, xsum, p.nb, B, K);
+  const int ld = L.kslice;  // staged row stride, in elements
+  if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
+  else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
+  else stage_x_affine<GS>(p.x, xs, xsum, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
+  if (cs > 1) cluster_sync_all();  // every CTA of the cluster is running before any DSMEM write
   __syncthreads();
 
-  float acc[B];
+  const uint32_t xs_a = smem_addr(xs);
+  const uint32_t xb = static_cast<uint32_t>(ld * T::kXBytes);   // bytes between batch rows
+  const uint32_t xsum_a = smem_addr(xsum);
+  const uint32_t sb_a = smem_addr(sb) + lane * L.sb_stride * 4;
+  bool ok = true;
+  int fail_stage = 0, fail_pending = 0;
+  uint32_t fail_phase = 0;
+  int consumed = 0;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int item = 0; item < nitems; ++item) {
+    const int row0 = (cluster + item * nclusters) * 32;
+    const int nvalid = min(32, p.N - row0);
+    if (F == kFmtAffineQ4 && item > 0) {
+      __syncthreads();
+      load_sb(row0);
+      __syncthreads();
+    }
+    float acc[B];
 #pragma unroll
-  for (int b = 0; b < B; ++b) acc[b] = 0.f;
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
 
-  const uint32_t* sb_row = sb + lane * L.sb_stride;
-  int i = 0;
-  for (; i < nmine; ++i) {
-    const int s = i % T::kStages;
-    const uint32_t parity = (i / T::kStages) & 1;
-    if (!mbar_wait(&bars[s], parity)) break;
-    const int c = warp + i * kGemvWarps;
-    const uint8_t* slot = ring + s * (32 * T::kSlotStride) + lane * T::kSlotStride;
-    if constexpr (F == kFmtQ4_0) chunk_q4_0<B>(slot, xs, K, c, acc);
-    else if constexpr (F == kFmtQ8_0) chunk_q8_0<B>(slot, xs, K, c, acc);
-    else chunk_affine<B, GS>(slot, xs, xsum, sb_row, K, c, acc);
-    __syncwarp();
-    const int inext = i + T::kStages;
-    if (inext < nmine) {
-      fence_proxy_async_smem();
-      issue(s, warp + inext * kGemvWarps);
+    for (int st = 0; st < nsteps; ++st) {
+      if (ok && !mbar_wait(&bars[stage], phase)) {
+        ok = false;
+        fail_stage = stage;
+        fail_phase = phase;
+        fail_pending = issued - consumed;  // copies issued and not yet consumed
+      }
+      ++consumed;
+      if (ok) {
+        const uint32_t slot = ring_a + stage * stage_bytes<F>(CP);
+        const int cl0 = wc0 + st * CP;  // slice-local chunk
+        const int nch = min(CP, mw - st * CP);
+#pragma unroll
+        for (int j = 0; j < T::kMaxCopyChunks; ++j) {
+          if (j < nch) {
+            const int cl = cl0 + j;
+            const uint32_t src = slot + j * (32 * T::kChunkBytes);
+            if constexpr (F == kFmtQ4_0) {
+              chunk_q4_0<B>(src, xs_a + cl * (kChunkCols * 2), xb, acc);
+            } else if constexpr (F == kFmtQ8_0) {
+              chunk_q8_0<B>(src, xs_a + cl * (kChunkCols * 4), xb, acc);
+            } else {
+              chunk_affine<B, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), xb, xsum_a,
+                                  (ld / GS) * 4, sb_a, cl * (kChunkCols / GS), acc);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (ok && issued < total) issue_next();
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+
+    // Reduce the 4 warps, then the cs CTAs of the cluster.
+    float* rd = red + (item & 1) * (kGemvWarps * B * 32);
+#pragma unroll
+    for (int b = 0; b < B; ++b) rd[(warp * B + b) * 32 + lane] = acc[b];
+    __syncthreads();
+    float* sl = slots + (item & 1) * (cs * B * 32);
+    for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {
+      const int b = idx >> 5;
+      const int l = idx & 31;
+      float v = 0.f;
+#pragma unroll
+      for (int wv = 0; wv < kGemvWarps; ++wv) v += rd[(wv * B + b) * 32 + l];
+      if (cs == 1) {
+        if (b < p.nb && l < nvalid) p.y[(size_t)b * p.N + row0 + l] = __float2half_rn(v);
+      } else {
+        st_cluster_f32(map_to_rank(sl + (crank * B + b) * 32 + l, 0), v);
+      }
+    }
+    if (cs > 1) {
+      cluster_sync_all();
+      if (crank == 0) {
+        for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {
+          const int b = idx >> 5;
+          const int l = idx & 31;
+          if (b < p.nb && l < nvalid) {
+            float v = 0.f;
+            for (int r = 0; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
+            p.y[(size_t)b * p.N + row0 + l] = __float2half_rn(v);
+          }
+        }
+      }
     }
   }
-  if (i < nmine) {
-    // A copy never completed.  Record it and wait (bounded) for the copies
-    // that are still in flight into this warp's ring before leaving.
-    if (lane == 0) record_device_error(kDevErrBarrierTimeout);
-    for (int j = i; j < min(nmine, i + T::kStages); ++j)
-      (void)mbar_wait(&bars[j % T::kStages], (j / T::kStages) & 1);
-  }
 
-#pragma unroll
-  for (int b = 0; b < B; ++b) red[(warp * B + b) * 32 + lane] = acc[b];
-  __syncthreads();
-  for (int t = threadIdx.x; t < B * 32; t += blockDim.x) {
-    const int b = t >> 5;
-    const int l = t & 31;
-    if (b < p.nb && l < nvalid) {
-      float sum = 0.f;
-#pragma unroll
-      for (int wv = 0; wv < kGemvWarps; ++wv) sum += red[(wv * B + b) * 32 + l];
-      p.y[(size_t)b * p.N + row0 + l] = __float2half_rn(sum);
+  if (!ok) {
+    // A copy never completed.  Record it and wait (bounded) for the copies
+    // still in flight into this warp's ring (at most S, starting with the one
+    // that timed out) before leaving.
+    if (lane == 0) record_device_error(kDevErrBarrierTimeout);
+    // The copies in flight were issued in ring order starting at the stage
+    // that timed out.
+    uint32_t ph = fail_phase;
+    int sidx = fail_stage;
+    for (int j = 0; j < fail_pending; ++j) {
+      (void)mbar_wait(&bars[sidx], ph);
+      if (++sidx == S) {
+        sidx = 0;
+        ph ^= 1;
+      }
     }
   }
 }
