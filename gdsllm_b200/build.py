@@ -50,7 +50,7 @@ def _run(cmd, verbose):
 
 
 def build_lib(force: bool = False, verbose: bool = True) -> Path:
-    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "gdsq.h"]
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
     if force or _newer(LIB_PATH, sources):
         BUILD.mkdir(parents=True, exist_ok=True)
         tmp = LIB_PATH.with_suffix(".so.tmp")

@@ -600,3 +600,47 @@ int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The reference's C++ launcher ABI (include/gdsq_reference_abi.h).
+
+#include "gdsq_reference_abi.h"
+
+namespace {
+void report(int status, const char* what) {
+  if (status != GDSQ_OK)
+    fprintf(stderr, "%s: %s (%s)\n", what, gdsq_status_string(status), gdsq_last_error());
+}
+}  // namespace
+
+void launch_fused_q4_0_gemv(const void* weight, const __half* x, __half* y, int out_dim, int in_dim,
+                            cudaStream_t stream) {
+  report(gdsq_fused_q4_0_gemv(weight, x, y, out_dim, in_dim, 1, stream), "fused_q4_0_gemv");
+}
+
+void launch_fused_q8_0_gemv(const void* weight, const __half* x, __half* y, int out_dim, int in_dim,
+                            cudaStream_t stream) {
+  report(gdsq_fused_q8_0_gemv(weight, x, y, out_dim, in_dim, 1, stream), "fused_q8_0_gemv");
+}
+
+void launch_dequant_q8_0(const void* src, __half* dst, size_t num_blocks, cudaStream_t stream) {
+  report(gdsq_dequant_q8_0(src, dst, num_blocks, stream), "dequant_q8_0");
+}
+
+void launch_dequant_q4_0(const void* src, __half* dst, size_t num_blocks, cudaStream_t stream) {
+  report(gdsq_dequant_q4_0(src, dst, num_blocks, stream), "dequant_q4_0");
+}
+
+void launch_dequant_affine_q4(const uint32_t* weight, const __half* scales, const __half* biases,
+                              __half* dst, size_t num_elements, int in_dim, int group_size,
+                              cudaStream_t stream) {
+  report(gdsq_dequant_affine_q4(weight, scales, biases, dst, num_elements, in_dim, group_size, stream),
+         "dequant_affine_q4");
+}
+
+void launch_fused_affine_q4_gemv(const uint32_t* weight, const __half* scales, const __half* biases,
+                                 const __half* x, __half* y, int out_dim, int in_dim, int group_size,
+                                 cudaStream_t stream) {
+  report(gdsq_fused_affine_q4_gemv(weight, scales, biases, x, y, out_dim, in_dim, group_size, 1, stream),
+         "fused_affine_q4_gemv");
+}

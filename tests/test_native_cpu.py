@@ -104,3 +104,46 @@ def test_empty_work_is_a_no_op():
     l = lib()
     assert l.gdsq_dequant_q4_0(None, None, 0, None) == 0
     assert l.gdsq_fused_q4_0_gemv(None, None, None, 0, 64, 1, None) == 0
+
+
+# Mangled names of the reference's launchers, as g++ produces them from
+# gdsllm/runtime/fused_gemv.h, gguf_dequant.h and affine_q4_dequant.h.
+REFERENCE_LAUNCHERS = [
+    "_Z19launch_dequant_q4_0PKvP6__halfmP11CUstream_st",
+    "_Z19launch_dequant_q8_0PKvP6__halfmP11CUstream_st",
+    "_Z22launch_fused_q4_0_gemvPKvPK6__halfPS1_iiP11CUstream_st",
+    "_Z22launch_fused_q8_0_gemvPKvPK6__halfPS1_iiP11CUstream_st",
+    "_Z24launch_dequant_affine_q4PKjPK6__halfS3_PS1_miiP11CUstream_st",
+    "_Z27launch_fused_affine_q4_gemvPKjPK6__halfS3_S3_PS1_iiiP11CUstream_st",
+]
+
+
+def test_reference_launcher_abi_is_exported():
+    import subprocess
+    from gdsllm_b200.build import LIB_PATH
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines()}
+    for name in REFERENCE_LAUNCHERS:
+        assert name in exported, name
+
+
+def test_cpp_caller_links_against_reference_abi(tmp_path):
+    """A C++ translation unit written against include/gdsq_reference_abi.h
+    (the reference's launcher declarations) links with libgdsq.so."""
+    import subprocess
+    from gdsllm_b200.build import BUILD
+    src = tmp_path / "caller.cpp"
+    src.write_text(
+        '#include "gdsq_reference_abi.h"\n'
+        "int main() {\n"
+        "  void* f[] = {(void*)&launch_fused_q4_0_gemv, (void*)&launch_fused_q8_0_gemv,\n"
+        "               (void*)&launch_dequant_q4_0, (void*)&launch_dequant_q8_0,\n"
+        "               (void*)&launch_dequant_affine_q4, (void*)&launch_fused_affine_q4_gemv};\n"
+        "  return f[0] == nullptr;\n"
+        "}\n")
+    exe = tmp_path / "caller"
+    subprocess.run(["g++", str(src), "-o", str(exe), f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
+                    f"-L{BUILD}", "-lgdsq", f"-Wl,-rpath,{BUILD}", "-Wl,--unresolved-symbols=ignore-in-shared-libs"],
+                   check=True, capture_output=True)
+    assert exe.exists()
