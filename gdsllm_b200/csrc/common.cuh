@@ -169,6 +169,91 @@ __device__ __forceinline__ float lds32f(uint32_t addr) {
   return v;
 }
 
+// ---- tcgen05 (5th-generation tensor core, tensor memory) ------------------
+// Tensor memory (TMEM) addresses are (lane << 16) | column.  A warp may touch
+// only the 32-lane quarter (warp_id % 4) of TMEM.
+
+// Allocates `ncols` TMEM columns for this CTA (warp-wide); the address is
+// written to shared memory at `dst`.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Each lane stores 16 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// Each lane loads 8 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+      : "r"(taddr)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem descriptor], kind::f16, issued by one thread.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// Arrives (once) on `bar` when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: 8 x 16-byte core
+// matrices; `lbo` = bytes between the two K halves of a core-matrix pair,
+// `sbo` = bytes between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;                // base offset 0, layout type 0 (no swizzle)
+}
+
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- fp16 bit tricks -------------------------------------------------------
 // The "magic number" conversion: OR-ing a 4-bit value n into the low mantissa
 // bits of fp16 1024.0 (0x6400) gives exactly 1024 + n, because the fp16 ulp in
@@ -190,6 +275,18 @@ __device__ __forceinline__ uint32_t h2_as_u32(__half2 v) {
 
 __device__ __forceinline__ uint32_t h2_const(float a, float b) {
   return h2_as_u32(__floats2half2_rn(a, b));
+}
+
+// Unpacks the 8 nibbles of one 32-bit word into 4 half2 of exact fp16
+// values, one LOP3 each: (1024 + n) for low nibbles, (1024 + 16 n) for high
+// nibbles.  Pair order as in unpack_nibbles_minus8.
+__device__ __forceinline__ void unpack_nibbles_biased(uint32_t q, uint32_t r[4]) {
+  const uint32_t kMagic = 0x64006400u;
+  const uint32_t q8 = q >> 8;
+  r[0] = lop3_and_or(q, 0x000F000Fu, kMagic);
+  r[1] = lop3_and_or(q, 0x00F000F0u, kMagic);
+  r[2] = lop3_and_or(q8, 0x000F000Fu, kMagic);
+  r[3] = lop3_and_or(q8, 0x00F000F0u, kMagic);
 }
 
 // Unpacks the 8 nibbles of one 32-bit word into 4 half2 values of (n - 8),

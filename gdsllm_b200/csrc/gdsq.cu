@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "dequant.cuh"
 #include "gemv.cuh"
+#include "gemv_tc.cuh"
 
 namespace gdsq {
 namespace {
@@ -140,14 +141,15 @@ struct MapKey {
   long long row_bytes;
   int n;
   int fmt;
+  int box_rows;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && row_bytes == o.row_bytes && n == o.n && fmt == o.fmt;
+    return ptr == o.ptr && row_bytes == o.row_bytes && n == o.n && fmt == o.fmt && box_rows == o.box_rows;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<long long>()(k.row_bytes) << 1) ^
-           ((size_t)k.n << 7) ^ ((size_t)k.fmt << 3);
+           ((size_t)k.n << 7) ^ ((size_t)k.fmt << 3) ^ ((size_t)k.box_rows << 40);
   }
 };
 std::mutex g_map_mutex;
@@ -155,9 +157,10 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps[kMaxDevices];
 constexpr size_t kMaxCachedMaps = 16384;
 
 template <int F>
-int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes, CUtensorMap* out) {
+int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes, CUtensorMap* out,
+               int box_rows = 32) {
   using T = GemvFormat<F>;
-  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, n, F};
+  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, n, F, box_rows};
   {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     auto it = g_maps[dev.ordinal].find(key);
@@ -172,7 +175,7 @@ int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes,
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)n};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {(cuuint32_t)(T::kChunkBytes / 8), 32};
+  const cuuint32_t box[2] = {(cuuint32_t)(T::kChunkBytes / 8), (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box,
                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -356,6 +359,97 @@ int launch_fast_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t s
   }
 }
 
+// Tensor-core Q4_0 GEMV (batch 1), opt-in with GDSQ_GEMV_TC=1: correct, but
+// on B200 its per-pair dequant -> MMA -> commit round trip makes it slower
+// than the CUDA-core kernel on the decode shapes, so it is not the default.
+bool tc_enabled() {
+  const char* e = getenv("GDSQ_GEMV_TC");
+  return e && e[0] == '1';
+}
+
+int launch_tc_q4_0(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
+  const int R = (p.N + kTcRows - 1) / kTcRows;
+  const int C = p.K / kChunkCols;
+  auto kernel = gemv_tc_q4_0_kernel;
+  int force_cs = 0, force_st = 0, force_cp = 0;
+  const bool forced = plan_override(&force_cs, &force_st, &force_cp);
+  // Largest cluster (<= 8, >= 2 chunks per CTA) whose grid still fits the
+  // GPU in one wave at the occupancy its shared memory allows; 2 stages.
+  int cs = 1, stages = 2;
+  const uint64_t key = ((uint64_t)1 << 62) | ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
+  bool cached = false;
+  if (!forced) {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = g_plans[dev.ordinal].find(key);
+    if (it != g_plans[dev.ordinal].end()) {
+      cs = it->second.cs;
+      stages = it->second.stages;
+      cached = true;
+    }
+  }
+  if (forced) {
+    cs = force_cs;
+    stages = force_st < 2 ? 2 : force_st;
+  } else if (!cached) {
+    const int cs_max = C / 2 < 1 ? 1 : (C / 2 > kMaxCluster ? kMaxCluster : C / 2);
+    for (int c = cs_max; c >= 1; --c) {
+      const TcLayout Lc = tc_layout(p.K, c, stages);
+      if (Lc.total > dev.smem_optin) continue;
+      cudaError_t e = ensure_smem(kernel, Lc.total, dev.ordinal);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tc)");
+      int occ = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kTcThreads, Lc.total);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      if ((long long)R * c <= (long long)dev.sms * occ) {
+        cs = c;
+        break;
+      }
+    }
+  }
+  if (!forced && !cached) {
+    GemvPlan plan;
+    plan.cs = cs;
+    plan.stages = stages;
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    g_plans[dev.ordinal][key] = plan;
+  }
+  const TcLayout L = tc_layout(p.K, cs, stages);
+  if (L.total > dev.smem_optin) return fail(GDSQ_ERR_UNSUPPORTED, "tensor-core GEMV does not fit shared memory");
+  CUtensorMap wmap;
+  int mst = weight_map<kFmtQ4_0>(dev, p.w, p.N, p.row_bytes, &wmap, kTcRows);
+  if (mst != GDSQ_OK) return mst;
+  cudaError_t e = ensure_smem(kernel, L.total, dev.ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tc)");
+  p.cs = cs;
+  p.stages = stages;
+  p.copy = 1;
+  p.num_rg = R;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(R * cs);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g_pdl_enabled) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv tc launch");
+  return GDSQ_OK;
+}
+
 template <int F>
 int launch_generic(const GemvParams& p, cudaStream_t stream) {
   const dim3 grid((p.N + 7) / 8);
@@ -433,6 +527,7 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
 
   const bool shape_ok = in_dim % kChunkCols == 0 && aligned(w, 16) && aligned(x, 16);
   if (fmt == kFmtQ4_0) {
+    if (shape_ok && batch == 1 && tc_enabled()) return launch_tc_q4_0(p, *dev, stream);
     if (shape_ok && fast_min_smem<kFmtQ4_0>(batch, in_dim, 0) <= dev->smem_optin)
       return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream);
     return launch_generic<kFmtQ4_0>(p, stream);

@@ -211,3 +211,14 @@ def test_affine_against_reference_kernels(gdsq, cuda, n, k, g):
     w16 = d_ref.cpu().numpy().reshape(n, k)
     _check_gemv(y_ours, w16, x, "ours")
     _check_gemv(y_ref, w16, x, "reference")
+
+
+@pytest.mark.parametrize("n,k", [(11008, 4096), (4096, 11008), (300, 1024), (128, 512)])
+def test_gemv_q4_0_tensor_core_kernel(gdsq, cuda, n, k, monkeypatch):
+    """The tcgen05 variant (opt-in) meets the same bar."""
+    monkeypatch.setenv("GDSQ_GEMV_TC", "1")
+    w = synth.q4_0_weight(n, k, seed=31)
+    x = synth.activations(1, k, seed=32).to(cuda)
+    y = gdsq.gemv_q4_0(w.to(cuda), x, n, k)
+    torch.cuda.synchronize()
+    _check_gemv(y, oracle.dequant_q4_0(w.numpy()).reshape(n, k), x, f"q4_0 tc {n}x{k}")
