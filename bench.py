@@ -25,6 +25,7 @@ as ``ref_cuda``.
 
 --gpus N (under torchrun): N independent replicas (weak scaling).
 --config 0: one 11008x4096 Q4_0 GEMV, rotating over copies larger than L2.
+--config 2: Q8_0 / affine-Q4 sweep (4 shapes x batch 1, 4, 8, 16).
 """
 from __future__ import annotations
 
@@ -531,13 +532,78 @@ def bench_config0(args, dist):
             "gpu_launches": launches, "clocks": clk}
 
 
+def bench_config2(args, dist):
+    """Q8_0 and affine-Q4 GEMV sweep: 4 shapes x batch 1/4/8/16 (BASELINE
+    config 2).  Each point is a CUDA graph of launches rotating over weight
+    copies that together exceed L2; value = aggregate GB/s over the sweep."""
+    from gdsllm_b200 import capi, lib as gdsq_lib
+    peak, peak_kind = load_peaks()
+    lib = gdsq_lib()
+    capi.set_pdl(bool(args.pdl))
+    shapes = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+    points = []
+    tot_bytes = 0.0
+    tot_ms = 0.0
+    launches = 0
+    for fmt in ("q8_0", "affine_q4"):
+        for n, k in shapes:
+            if fmt == "q8_0":
+                wbytes = q8_bytes(n, k)
+            else:
+                wbytes = n * k // 2 + 2 * 2 * n * (k // 128)
+            copies = max(2, int(300e6 // wbytes) + 1)
+            if fmt == "q8_0":
+                ws = [(synth.q8_0_weight(n, k, seed=i, device=dist.device),) for i in range(copies)]
+            else:
+                ws = [synth.affine_q4_weight(n, k, seed=i, device=dist.device) for i in range(copies)]
+            for b in (1, 4, 8, 16):
+                x = synth.activations(b, k, seed=5, device=dist.device)
+                y = torch.empty(b, n, dtype=torch.float16, device=dist.device)
+
+                def fn(stream, ws=ws, x=x, y=y, n=n, k=k, b=b, fmt=fmt):
+                    for w in ws:
+                        if fmt == "q8_0":
+                            st = lib.gdsq_fused_q8_0_gemv(w[0].data_ptr(), x.data_ptr(), y.data_ptr(), n, k, b,
+                                                          stream)
+                        else:
+                            st = lib.gdsq_fused_affine_q4_gemv(w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),
+                                                               x.data_ptr(), y.data_ptr(), n, k, 128, b, stream)
+                        if st:
+                            raise RuntimeError(lib.gdsq_last_error().decode())
+
+                g = capture(fn)
+                reps = max(3, args.steps // copies)
+                ms, _ = time_graph(g, reps, args.warmup, dist)
+                us = ms * 1e3 / (reps * copies)
+                alg = wbytes + 2 * b * (k + n)
+                gbs = alg / (us / 1e6) / 1e9
+                points.append({"fmt": fmt, "n": n, "k": k, "batch": b, "us": round(us, 3),
+                               "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+                tot_bytes += alg * reps * copies
+                tot_ms += ms
+                launches += reps * copies
+                del g
+            del ws
+            torch.cuda.empty_cache()
+    agg = tot_bytes / (tot_ms / 1e3) / 1e9
+    return {"metric": "Q8_0 / affine-Q4 fused dequant-GEMV sweep, aggregate HBM GB/s", "value": round(agg, 1),
+            "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(tot_ms / max(1, launches), 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config 2: 4 shapes x batch 1/4/8/16, Q8_0 and affine-Q4 g=128",
+                       "l2": "rotating over weight copies > 300 MB per point"},
+            "roofline": {"bound": "hbm", "achieved": round(agg, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(agg / peak, 4), "peak_kind": peak_kind},
+            "sweep": points, "gpu_launches": launches}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1])
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2])
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
@@ -549,6 +615,8 @@ def main():
             res = bench_reference(args, dist)
         elif args.config == 0:
             res = bench_config0(args, dist)
+        elif args.config == 2:
+            res = bench_config2(args, dist)
         else:
             res = bench_ours(args, dist)
         if dist.rank == 0 and res is not None:

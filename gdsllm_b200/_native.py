@@ -30,6 +30,10 @@ _C_SIGNATURES = {
                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                  ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  ctypes.c_void_p]),
+    "gdsq_moe_affine_q4_gate_up": (ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int] * 8
+                                   + [ctypes.c_void_p]),
+    "gdsq_moe_affine_q4_down": (ctypes.c_int, [ctypes.c_void_p] * 7 + [ctypes.c_int] * 9
+                                + [ctypes.c_void_p]),
 }
 
 

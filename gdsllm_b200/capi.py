@@ -80,3 +80,43 @@ def gemv_affine_q4(words, scales, biases, x: torch.Tensor, n: int, k: int, group
     check(lib().gdsq_fused_affine_q4_gemv(_p(words), _p(scales), _p(biases), _p(x), _p(out), n, k,
                                           group, b, _stream(x)), "gdsq_fused_affine_q4_gemv")
     return out
+
+
+MOE_OUT_F32 = 1      # GDSQ_MOE_OUT_F32
+MOE_ACCUMULATE = 2   # GDSQ_MOE_ACCUMULATE
+
+
+def moe_gate_up(gate, up, x: torch.Tensor, ids: torch.Tensor, group: int, expert_first: int = 0,
+                expert_total: int | None = None, out=None) -> torch.Tensor:
+    """h [ntok, top_k, inter] = fp16(silu(gate_e x) * up_e x) for e = ids.
+    gate / up: (words int32 [E, inter, hidden/8], scales, biases); ids int32
+    [ntok, top_k]."""
+    gw, gs, gb = gate
+    uw, us, ub = up
+    e, inter, hidden = gw.shape[0], gw.shape[1], gw.shape[2] * 8
+    ntok, top_k = ids.shape
+    total = expert_first + e if expert_total is None else expert_total
+    if out is None:
+        out = torch.empty((ntok, top_k, inter), dtype=torch.float16, device=x.device)
+    check(lib().gdsq_moe_affine_q4_gate_up(_p(gw), _p(gs), _p(gb), _p(uw), _p(us), _p(ub), _p(x), _p(ids),
+                                           _p(out), ntok, top_k, inter, hidden, group, expert_first, e,
+                                           total, _stream(x)), "gdsq_moe_affine_q4_gate_up")
+    return out
+
+
+def moe_down(down, h: torch.Tensor, ids: torch.Tensor, route: torch.Tensor, group: int,
+             expert_first: int = 0, expert_total: int | None = None, out=None, flags: int = 0) -> torch.Tensor:
+    """y [ntok, hidden] = sum_k route[:, k] * down_e h[:, k] (fp32 sum).
+    down: (words int32 [E, hidden, inter/8], scales, biases); route fp16
+    [ntok, top_k]."""
+    dw, ds, db = down
+    e, hidden, inter = dw.shape[0], dw.shape[1], dw.shape[2] * 8
+    ntok, top_k = ids.shape
+    total = expert_first + e if expert_total is None else expert_total
+    if out is None:
+        dt = torch.float32 if flags & MOE_OUT_F32 else torch.float16
+        out = torch.empty((ntok, hidden), dtype=dt, device=h.device)
+    check(lib().gdsq_moe_affine_q4_down(_p(dw), _p(ds), _p(db), _p(h), _p(ids), _p(route), _p(out), ntok,
+                                        top_k, hidden, inter, group, expert_first, e, total, flags,
+                                        _stream(h)), "gdsq_moe_affine_q4_down")
+    return out

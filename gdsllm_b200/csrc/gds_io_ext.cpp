@@ -36,6 +36,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "gdsq.h"
@@ -485,6 +486,117 @@ torch::Tensor py_fused_affine_q4_gemv(Handle h, torch::Tensor x, std::vector<int
   return out;
 }
 
+// Additive op (no reference counterpart as one call): the routed-expert part
+// of moe_mlp_selective's decode branch, gdsllm/runtime/qwen_moe.py:453-474,
+// with expert ids and routing weights left in device memory.
+// gate/up/down = (words int32 [E, rows, cols/8], scales fp16 [E, rows,
+// cols/group], biases fp16), experts expert_first .. expert_first+E-1 of
+// expert_total.  Returns y with x's shape (fp16, or fp32 with out_fp32).
+using ExpertStack = std::tuple<torch::Tensor, torch::Tensor, torch::Tensor>;
+
+void check_stack(const ExpertStack& m, const char* what, int64_t rows, int64_t cols, int group,
+                 int64_t experts, const torch::Device& dev) {
+  const auto& w = std::get<0>(m);
+  const auto& sc = std::get<1>(m);
+  const auto& bi = std::get<2>(m);
+  const std::string op = std::string("fused_moe_affine_q4: ") + what;
+  for (const torch::Tensor* t : {&w, &sc, &bi}) {
+    if (!t->is_cuda() || t->device() != dev) throw std::runtime_error(op + " tensors must be on " + dev.str());
+    if (!t->is_contiguous()) throw std::runtime_error(op + " tensors must be contiguous");
+    if (t->dim() != 3) throw std::runtime_error(op + " tensors must be 3-D [experts, rows, ...]");
+  }
+  if (w.scalar_type() != torch::kInt32 && w.scalar_type() != torch::kUInt32)
+    throw std::runtime_error(op + " weight must be int32/uint32 packed words");
+  if (sc.scalar_type() != torch::kFloat16 || bi.scalar_type() != torch::kFloat16)
+    throw std::runtime_error(op + " scales and biases must be float16");
+  if (w.size(0) != experts || w.size(1) != rows || w.size(2) != cols / 8)
+    throw std::runtime_error(op + " weight shape must be [" + std::to_string(experts) + ", " + std::to_string(rows) +
+                             ", " + std::to_string(cols / 8) + "]");
+  const std::vector<int64_t> gshape = {experts, rows, cols / group};
+  if (sc.sizes().vec() != gshape || bi.sizes().vec() != gshape)
+    throw std::runtime_error(op + " scales/biases shape must be [" + std::to_string(experts) + ", " +
+                             std::to_string(rows) + ", " + std::to_string(cols / group) + "]");
+}
+
+torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, torch::Tensor route_weights,
+                                     ExpertStack gate, ExpertStack up, ExpertStack down, int group_size,
+                                     int64_t expert_first, int64_t expert_total,
+                                     c10::optional<torch::Tensor> out, bool accumulate, bool out_fp32,
+                                     c10::optional<torch::Tensor> h) {
+  const char* op = "fused_moe_affine_q4";
+  if (!x.is_cuda() || x.scalar_type() != torch::kFloat16)
+    throw std::runtime_error("fused_moe_affine_q4: x must be a CUDA float16 tensor");
+  const torch::Device dev = x.device();
+  if (!expert_ids.is_cuda() || expert_ids.device() != dev || expert_ids.dim() < 1)
+    throw std::runtime_error("fused_moe_affine_q4: expert_ids must be a CUDA tensor [..., top_k] on x's device");
+  if (expert_ids.scalar_type() != torch::kInt32 && expert_ids.scalar_type() != torch::kInt64)
+    throw std::runtime_error("fused_moe_affine_q4: expert_ids must be int32 or int64");
+  const int64_t top_k = expert_ids.size(-1);
+  const int64_t ntok = top_k > 0 ? expert_ids.numel() / top_k : 0;
+  const auto& gw = std::get<0>(gate);
+  if (gw.dim() != 3) throw std::runtime_error("fused_moe_affine_q4: gate weight must be 3-D");
+  const int64_t experts = gw.size(0);
+  const int64_t inter = gw.size(1);
+  const int64_t hidden = gw.size(2) * 8;
+  if (group_size <= 0 || group_size % 8 != 0 || hidden % group_size != 0 || inter % group_size != 0)
+    throw std::runtime_error("fused_moe_affine_q4: group_size " + std::to_string(group_size) +
+                             " must be a multiple of 8 dividing hidden " + std::to_string(hidden) +
+                             " and intermediate " + std::to_string(inter));
+  check_stack(gate, "gate", inter, hidden, group_size, experts, dev);
+  check_stack(up, "up", inter, hidden, group_size, experts, dev);
+  check_stack(down, "down", hidden, inter, group_size, experts, dev);
+  if (x.numel() != ntok * hidden)
+    throw std::runtime_error("fused_moe_affine_q4: x has " + std::to_string(x.numel()) + " elements, expected " +
+                             std::to_string(ntok) + " tokens x " + std::to_string(hidden));
+  if (route_weights.numel() != ntok * top_k || !route_weights.is_cuda() || route_weights.device() != dev)
+    throw std::runtime_error("fused_moe_affine_q4: route_weights must be a CUDA tensor with one weight per id");
+  if (expert_total < 0) expert_total = expert_first + experts;
+  c10::cuda::CUDAGuard guard(dev);
+  void* stream = c10::cuda::getCurrentCUDAStream(dev.index()).stream();
+  torch::Tensor ids = expert_ids.to(torch::kInt32).contiguous();
+  torch::Tensor rw = route_weights.to(torch::kFloat16).contiguous();
+  torch::Tensor xc = x.contiguous();
+  const auto out_dtype = out_fp32 ? torch::kFloat32 : torch::kFloat16;
+  torch::Tensor y;
+  if (out.has_value()) {
+    y = *out;
+    if (!y.is_cuda() || y.device() != dev || y.scalar_type() != out_dtype || !y.is_contiguous() ||
+        y.numel() != ntok * hidden)
+      throw std::runtime_error(std::string("fused_moe_affine_q4: out must be a contiguous ") +
+                               (out_fp32 ? "float32" : "float16") + " CUDA tensor of " +
+                               std::to_string(ntok * hidden) + " elements");
+  } else {
+    if (accumulate) throw std::runtime_error("fused_moe_affine_q4: accumulate=True needs out");
+    y = torch::empty(x.sizes(), x.options().dtype(out_dtype));
+  }
+  torch::Tensor hb;
+  if (h.has_value()) {
+    hb = *h;
+    if (!hb.is_cuda() || hb.device() != dev || hb.scalar_type() != torch::kFloat16 || !hb.is_contiguous() ||
+        hb.numel() < ntok * top_k * inter)
+      throw std::runtime_error("fused_moe_affine_q4: h must be a contiguous float16 CUDA tensor of at least " +
+                               std::to_string(ntok * top_k * inter) + " elements");
+  } else {
+    hb = torch::empty({ntok, top_k, inter}, x.options());
+  }
+  int st = gdsq_moe_affine_q4_gate_up(
+      gw.data_ptr(), std::get<1>(gate).data_ptr(), std::get<2>(gate).data_ptr(), std::get<0>(up).data_ptr(),
+      std::get<1>(up).data_ptr(), std::get<2>(up).data_ptr(), xc.data_ptr(), ids.data_ptr<int32_t>(),
+      hb.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k), static_cast<int>(inter),
+      static_cast<int>(hidden), group_size, static_cast<int>(expert_first), static_cast<int>(experts),
+      static_cast<int>(expert_total), stream);
+  raise_status(st, op);
+  const int flags = (out_fp32 ? GDSQ_MOE_OUT_F32 : 0) | (accumulate ? GDSQ_MOE_ACCUMULATE : 0);
+  st = gdsq_moe_affine_q4_down(std::get<0>(down).data_ptr(), std::get<1>(down).data_ptr(),
+                               std::get<2>(down).data_ptr(), hb.data_ptr(), ids.data_ptr<int32_t>(),
+                               rw.data_ptr(), y.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k),
+                               static_cast<int>(hidden), static_cast<int>(inter), group_size,
+                               static_cast<int>(expert_first), static_cast<int>(experts),
+                               static_cast<int>(expert_total), flags, stream);
+  raise_status(st, op);
+  return y;
+}
+
 int py_device_error(int device, bool clear) {
   int bits = 0;
   raise_status(gdsq_device_error(device, clear ? 1 : 0, &bits), "device_error");
@@ -535,6 +647,13 @@ PYBIND11_MODULE(gds_io_ext, m) {
         py::arg("handle"), py::arg("x"), py::arg("weight_shape"), py::arg("weight_offset"),
         py::arg("scale_offset"), py::arg("bias_offset"), py::arg("group_size"));
 
+  m.def("fused_moe_affine_q4", &py_fused_moe_affine_q4,
+        "Routed-expert MLP of a MoE layer (decode): gate/up + SiLU*mul, then down with the routing-weighted "
+        "sum, expert ids read on the device.",
+        py::arg("x"), py::arg("expert_ids"), py::arg("route_weights"), py::arg("gate"), py::arg("up"),
+        py::arg("down"), py::arg("group_size") = 128, py::arg("expert_first") = 0, py::arg("expert_total") = -1,
+        py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("out_fp32") = false,
+        py::arg("h") = py::none());
   m.def("handle_from_tensor", &GdsBufferHandle::wrap,
         "Wrap a contiguous CUDA tensor as a GdsBufferHandle (the tensor stays alive with the handle).",
         py::arg("tensor"));

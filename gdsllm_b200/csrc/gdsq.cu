@@ -19,6 +19,7 @@
 #include "dequant.cuh"
 #include "gemv.cuh"
 #include "gemv_tc.cuh"
+#include "moe.cuh"
 
 namespace gdsq {
 namespace {
@@ -142,14 +143,16 @@ struct MapKey {
   int n;
   int fmt;
   int box_rows;
+  int depth;  // experts of a 3-D map (1 for a 2-D weight matrix)
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && row_bytes == o.row_bytes && n == o.n && fmt == o.fmt && box_rows == o.box_rows;
+    return ptr == o.ptr && row_bytes == o.row_bytes && n == o.n && fmt == o.fmt && box_rows == o.box_rows &&
+           depth == o.depth;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<long long>()(k.row_bytes) << 1) ^
-           ((size_t)k.n << 7) ^ ((size_t)k.fmt << 3) ^ ((size_t)k.box_rows << 40);
+           ((size_t)k.n << 7) ^ ((size_t)k.fmt << 3) ^ ((size_t)k.box_rows << 40) ^ ((size_t)k.depth << 50);
   }
 };
 std::mutex g_map_mutex;
@@ -160,7 +163,7 @@ template <int F>
 int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes, CUtensorMap* out,
                int box_rows = 32) {
   using T = GemvFormat<F>;
-  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, n, F, box_rows};
+  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, n, F, box_rows, 1};
   {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     auto it = g_maps[dev.ordinal].find(key);
@@ -184,6 +187,42 @@ int weight_map(const DeviceInfo& dev, const void* w, int n, long long row_bytes,
   if (r != CUDA_SUCCESS)
     return fail(GDSQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for a %d x %lld-byte weight", (int)r, n,
                 row_bytes);
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  if (g_maps[dev.ordinal].size() >= kMaxCachedMaps) g_maps[dev.ordinal].clear();
+  g_maps[dev.ordinal][key] = map;
+  *out = map;
+  return GDSQ_OK;
+}
+
+// Stacked affine-Q4 experts [experts][rows][cols/8 words] as a 3-D tensor of
+// 8-byte elements; one box is box_rows rows x one 256-column chunk (128 B,
+// 128-byte swizzle) of one expert.
+int expert_map(const DeviceInfo& dev, const void* w, int experts, int rows, int cols, int box_rows,
+               CUtensorMap* out) {
+  const long long row_bytes = cols / 2;
+  const MapKey key{reinterpret_cast<uintptr_t>(w), row_bytes, rows, 16, box_rows, experts};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    auto it = g_maps[dev.ordinal].find(key);
+    if (it != g_maps[dev.ordinal].end()) {
+      *out = it->second;
+      return GDSQ_OK;
+    }
+  }
+  PFN_cuTensorMapEncodeTiled_v12000 encode;
+  int st = get_encoder(&encode);
+  if (st != GDSQ_OK) return st;
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows, (cuuint64_t)experts};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_bytes * rows};
+  const cuuint32_t box[3] = {(cuuint32_t)(kMoeChunkBytes / 8), (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(w), dims, strides, box,
+                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(GDSQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %d experts of %d x %d", (int)r,
+                experts, rows, cols);
   std::lock_guard<std::mutex> lock(g_map_mutex);
   if (g_maps[dev.ordinal].size() >= kMaxCachedMaps) g_maps[dev.ordinal].clear();
   g_maps[dev.ordinal][key] = map;
@@ -550,6 +589,232 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
 }
 
 // ---------------------------------------------------------------------------
+// MoE gather dispatch
+
+struct MoePlan {
+  int cs = 1;
+  int stages = 2;
+  int nclusters = 1;
+  int smem = 0;
+};
+
+// Same cost model as make_plan, over `items` work items of C chunks each.
+template <int STAGE, int GS>
+int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
+  auto kernel = moe_affine_kernel<STAGE, GS>;
+  int force_cs = 0, force_st = 0;
+  bool forced = false;
+  if (const char* e = getenv("GDSQ_MOE_PLAN")) {
+    forced = sscanf(e, "%d:%d", &force_cs, &force_st) == 2 && force_cs >= 1 && force_cs <= kMaxCluster &&
+             force_st >= 1 && force_st <= kMaxStages;
+  }
+  double best = 1e30;
+  bool found = false;
+  for (int cs = 1; cs <= kMaxCluster; cs *= 2) {
+    if (cs > C) break;
+    if (forced && cs != force_cs) continue;
+    const int cslice = (C + cs - 1) / cs;
+    for (int st = 2; st <= 4; ++st) {
+      if (forced && st != force_st) continue;
+      const MoeSmemLayout L = moe_smem_layout(C, GS, cs, st);
+      if (L.total > dev.smem_optin) continue;
+      cudaError_t e = ensure_smem(kernel, L.total, dev.ordinal);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(moe)");
+      int occ = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, L.total);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      if (occ < 1) continue;
+      const long long slots = (long long)dev.sms * occ;
+      const long long ctas = (long long)items * cs;
+      double load;
+      long long resident;
+      int nclusters;
+      if (ctas <= slots) {
+        nclusters = items;
+        resident = (ctas + dev.sms - 1) / dev.sms;
+        load = (double)resident * (cslice + 1);
+      } else {
+        nclusters = (int)(slots / cs);
+        const int per = (items + nclusters - 1) / nclusters;
+        resident = occ;
+        load = (double)occ * per * (cslice + 1);
+      }
+      const double warps = (double)resident * kGemvWarps;
+      const double eff = warps >= 16 ? 1.0 : warps / 16.0;
+      const double cost = load / eff * (1.0 + 0.02 * cs) / (1.0 + 0.01 * st);
+      if (cost < best) {
+        best = cost;
+        found = true;
+        out->cs = cs;
+        out->stages = st;
+        out->nclusters = nclusters;
+        out->smem = L.total;
+      }
+    }
+  }
+  if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no MoE launch plan fits shared memory");
+  return GDSQ_OK;
+}
+
+template <int STAGE, int GS>
+int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const DeviceInfo& dev,
+                    cudaStream_t stream) {
+  const int cpe = p.K / kChunkCols;
+  const int C = STAGE == 0 ? cpe : p.T * cpe;
+  p.num_items = STAGE == 0 ? p.ntok * p.T * (p.rows / 16) : p.ntok * (p.rows / 32);
+  const uint64_t key = ((uint64_t)1 << 63) | ((uint64_t)STAGE << 61) | ((uint64_t)GS << 50) |
+                       ((uint64_t)(unsigned)p.num_items << 16) | (uint64_t)(unsigned)C;
+  MoePlan plan;
+  bool have = false;
+  static std::unordered_map<uint64_t, MoePlan> plans[kMaxDevices];
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = plans[dev.ordinal].find(key);
+    if (it != plans[dev.ordinal].end()) {
+      plan = it->second;
+      have = true;
+    }
+  }
+  if (!have) {
+    int st = make_moe_plan<STAGE, GS>(p.num_items, C, dev, &plan);
+    if (st != GDSQ_OK) return st;
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    plans[dev.ordinal][key] = plan;
+  }
+  CUtensorMap m0, m1;
+  const int box_rows = STAGE == 0 ? 16 : 32;
+  int st = expert_map(dev, w0, p.e_count, p.rows, p.K, box_rows, &m0);
+  if (st != GDSQ_OK) return st;
+  if (STAGE == 0) {
+    st = expert_map(dev, w1, p.e_count, p.rows, p.K, box_rows, &m1);
+    if (st != GDSQ_OK) return st;
+  } else {
+    m1 = m0;
+  }
+  auto kernel = moe_affine_kernel<STAGE, GS>;
+  cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(moe)");
+  p.cs = plan.cs;
+  p.stages = plan.stages;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.nclusters * plan.cs);
+  cfg.blockDim = dim3(kGemvWarps * 32);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (plan.cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = plan.cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g_pdl_enabled) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kernel, p, m0, m1);
+  if (e != cudaSuccess) return cuda_fail(e, STAGE == 0 ? "moe gate/up launch" : "moe down launch");
+  return GDSQ_OK;
+}
+
+// Shared argument checks and path choice of both MoE stages.  Matrix 0 is
+// gate (stage 0) or down (stage 1); matrix 1 is up (stage 0 only).
+int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, const void* w1,
+                 const void* s1, const void* b1, const void* x, const int32_t* ids,
+                 const void* route, void* out, int ntok, int top_k, int rows, int cols, int group,
+                 int e_first, int e_count, int e_total, int flags, void* stream_v) {
+  t_last_error.clear();
+  const char* name = stage == 0 ? "moe gate/up" : "moe down";
+  if (ntok < 0 || top_k < 1 || top_k > kMoeMaxSlots)
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: num_tokens %d must be >= 0 and top_k %d in 1..%d", name, ntok,
+                top_k, kMoeMaxSlots);
+  if (rows <= 0 || cols <= 0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: expert matrix shape [%d, %d] must be positive", name, rows, cols);
+  if (group <= 0 || group % 8 != 0 || cols % group != 0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: group_size %d must be a positive multiple of 8 dividing %d", name,
+                group, cols);
+  if (e_first < 0 || e_count < 1 || e_total < 1 || (long long)e_first + e_count > e_total)
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: resident experts [%d, %d) outside 0..%d", name, e_first,
+                e_first + e_count, e_total);
+  if (flags & ~(kMoeOutF32 | kMoeAccumulate))
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: unknown flags 0x%x", name, flags);
+  const long long pairs = (long long)ntok * top_k;
+  if (pairs * rows > (1ll << 30))
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: %lld outputs is too many for one call", name, pairs * rows);
+  if (ntok == 0) return GDSQ_OK;
+  if (!w0 || !s0 || !b0 || !x || !ids || !out || (stage == 0 && (!w1 || !s1 || !b1)) || (stage == 1 && !route))
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: null pointer", name);
+  if (!aligned(w0, 4) || (stage == 0 && !aligned(w1, 4)))
+    return fail(GDSQ_ERR_MISALIGNED, "%s: expert weights must be 4-byte aligned", name);
+  if (!aligned(s0, 2) || !aligned(b0, 2) || (stage == 0 && (!aligned(s1, 2) || !aligned(b1, 2))) ||
+      !aligned(x, 2) || (stage == 1 && !aligned(route, 2)))
+    return fail(GDSQ_ERR_MISALIGNED, "%s: scales, biases, activations and weights of the route need 2-byte alignment",
+                name);
+  if (!aligned(ids, 4)) return fail(GDSQ_ERR_MISALIGNED, "%s: expert ids must be 4-byte aligned", name);
+  if (!aligned(out, (stage == 1 && (flags & kMoeOutF32)) ? 4 : 2))
+    return fail(GDSQ_ERR_MISALIGNED, "%s: output misaligned", name);
+
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+
+  MoeParams p = {};
+  p.s0 = static_cast<const __half*>(s0);
+  p.b0 = static_cast<const __half*>(b0);
+  p.s1 = static_cast<const __half*>(s1);
+  p.b1 = static_cast<const __half*>(b1);
+  p.x = static_cast<const __half*>(x);
+  p.ids = ids;
+  p.route = static_cast<const __half*>(route);
+  p.out = out;
+  p.ntok = ntok;
+  p.T = top_k;
+  p.e_first = e_first;
+  p.e_count = e_count;
+  p.e_total = e_total;
+  p.rows = rows;
+  p.K = cols;
+  p.flags = stage == 1 ? flags : 0;
+  p.w0 = static_cast<const uint32_t*>(w0);
+  p.w1 = static_cast<const uint32_t*>(w1);
+  p.group = group;
+
+  const bool fast = cols % kChunkCols == 0 && rows % (stage == 0 ? 16 : 32) == 0 && aligned(w0, 16) &&
+                    (stage == 1 || aligned(w1, 16)) && aligned(x, 16) &&
+                    (group == 32 || group == 64 || group == 128 || group == 256) &&
+                    moe_smem_layout(stage == 0 ? cols / kChunkCols : top_k * cols / kChunkCols, group,
+                                    kMaxCluster, 2).total <= dev->smem_optin;
+  if (fast) {
+    if (stage == 0) {
+      switch (group) {
+        case 32: return launch_moe_fast<0, 32>(p, w0, w1, *dev, stream);
+        case 64: return launch_moe_fast<0, 64>(p, w0, w1, *dev, stream);
+        case 128: return launch_moe_fast<0, 128>(p, w0, w1, *dev, stream);
+        default: return launch_moe_fast<0, 256>(p, w0, w1, *dev, stream);
+      }
+    }
+    switch (group) {
+      case 32: return launch_moe_fast<1, 32>(p, w0, w1, *dev, stream);
+      case 64: return launch_moe_fast<1, 64>(p, w0, w1, *dev, stream);
+      case 128: return launch_moe_fast<1, 128>(p, w0, w1, *dev, stream);
+      default: return launch_moe_fast<1, 256>(p, w0, w1, *dev, stream);
+    }
+  }
+  const long long warps = stage == 0 ? pairs * rows : (long long)ntok * rows;
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
+  cudaError_t e = stage == 0 ? launch(moe_gate_up_generic_kernel, grid, dim3(256), 0, stream, g_pdl_enabled != 0, p)
+                             : launch(moe_down_generic_kernel, grid, dim3(256), 0, stream, g_pdl_enabled != 0, p);
+  if (e != cudaSuccess) return cuda_fail(e, stage == 0 ? "moe gate/up (generic) launch" : "moe down (generic) launch");
+  return GDSQ_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Dequant dispatch
 
 unsigned dequant_grid(uint64_t units, const DeviceInfo& dev) {
@@ -692,6 +957,25 @@ int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void
                               int batch, void* stream) {
   return gemv_dispatch(kFmtAffineQ4, weight, scales, biases, x, y, out_dim, in_dim, group_size,
                        batch, stream);
+}
+
+int gdsq_moe_affine_q4_gate_up(const void* gate_weight, const void* gate_scales, const void* gate_biases,
+                               const void* up_weight, const void* up_scales, const void* up_biases,
+                               const void* x, const int32_t* expert_ids, void* h, int num_tokens, int top_k,
+                               int inter_dim, int hidden_dim, int group_size, int expert_first,
+                               int expert_count, int expert_total, void* stream) {
+  return moe_dispatch(0, gate_weight, gate_scales, gate_biases, up_weight, up_scales, up_biases, x,
+                      expert_ids, nullptr, h, num_tokens, top_k, inter_dim, hidden_dim, group_size,
+                      expert_first, expert_count, expert_total, 0, stream);
+}
+
+int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales, const void* down_biases,
+                            const void* h, const int32_t* expert_ids, const void* route_weights, void* y,
+                            int num_tokens, int top_k, int hidden_dim, int inter_dim, int group_size,
+                            int expert_first, int expert_count, int expert_total, int flags, void* stream) {
+  return moe_dispatch(1, down_weight, down_scales, down_biases, nullptr, nullptr, nullptr, h, expert_ids,
+                      route_weights, y, num_tokens, top_k, hidden_dim, inter_dim, group_size, expert_first,
+                      expert_count, expert_total, flags, stream);
 }
 
 }  // extern "C"

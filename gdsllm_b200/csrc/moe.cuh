@@ -1,0 +1,469 @@
+// Fused mixture-of-experts gather over affine-Q4 experts, for decode.
+//
+// Replaces the per-slot decode loop of moe_mlp_selective
+// (gdsllm/runtime/qwen_moe.py:453-474).  The reference, for each of the
+// top-k slots, reads the expert id back to the host (`.item()`), runs three
+// fused GEMVs (affine_q4_dequant.cu:79-158) and does SiLU, the product and
+// the routing-weighted sum as separate torch ops.  Here, for token b and
+// slot t with expert e = ids[b][t] (device memory, never read by the host):
+//
+//   stage 0:  h[b][t] = fp16( silu(fp16(gate_e . x_b)) * fp16(up_e . x_b) )
+//   stage 1:  y[b]    = sum_t  w[b][t] * (down_e . h[b][t])      (fp32 sum)
+//
+// with silu(v) = v / (1 + exp(-v)) evaluated in fp32 on the fp16 value, the
+// rounding sequence of F.silu(gate_out) * up_out on fp16 tensors.  Stage 1
+// keeps the slot sum in fp32 and rounds once; the reference rounds every
+// slot's product and running sum to fp16 (qwen_moe.py:474).
+//
+// Experts are stacked [E][rows][K/8] uint32 words with [E][rows][K/GS] fp16
+// scales and biases (the layer-file layout, convert_qwen_moe.py:205-253).
+// Only experts [e_first, e_first + e_count) are resident (expert parallelism:
+// each rank holds a contiguous range); slots whose expert lives elsewhere are
+// skipped, so stage 1 yields this rank's partial sum.
+//
+// Schedule (same machinery as the dense fast GEMV in gemv.cuh):
+//   * Work item = 32 output lanes.  Stage 0: rows [r0, r0+16) of gate (lanes
+//     0..15) and of up (lanes 16..31) for one (token, slot) pair, so the SiLU
+//     product is formed in the epilogue of the item that computed both.
+//     Stage 1: rows [r0, r0+32) of down for one token, K running over the
+//     token's T slots back to back (chunk c belongs to slot c / (K/256)).
+//   * K is split across a thread-block cluster (cs CTAs, DSMEM reduction to
+//     the leader); each warp streams its 256-column chunks through a private
+//     ring fed by 3-D TMA boxes whose z coordinate is the local expert index.
+//     Chunks of non-resident experts are never fetched.
+//   * Activations (x of the token, or h of the token's slots) are staged in
+//     shared memory in the dequantizer's pair order once per token.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace gdsq {
+
+constexpr int kMoeMaxSlots = 64;           // top-k limit of one token
+constexpr int kMoeChunkBytes = 128;        // one 256-column chunk of one row
+constexpr int kMoeStageBytes = 32 * kMoeChunkBytes;
+enum : int { kMoeOutF32 = 1, kMoeAccumulate = 2 };
+
+struct MoeParams {
+  const __half* s0;     // scales of matrix 0 (gate in stage 0, down in stage 1)
+  const __half* b0;     // biases of matrix 0
+  const __half* s1;     // scales of matrix 1 (up; stage 0 only)
+  const __half* b1;
+  const __half* x;      // stage 0: tokens [ntok][K]; stage 1: h [ntok][T][K]
+  const int* ids;       // [ntok][T] global expert ids
+  const __half* route;  // [ntok][T] routing weights (stage 1)
+  void* out;            // stage 0: h fp16 [ntok][T][rows]; stage 1: y [ntok][rows]
+  int ntok;
+  int T;
+  int e_first;          // first resident expert
+  int e_count;          // resident experts
+  int e_total;          // valid ids are 0 .. e_total-1
+  int rows;             // rows of one expert matrix
+  int K;                // columns of one expert matrix
+  int cs;
+  int stages;
+  int num_items;
+  int flags;            // stage 1: kMoeOutF32 | kMoeAccumulate
+  // Generic kernels only: packed words of the matrices (the fast kernels
+  // read them through tensor maps).
+  const uint32_t* w0;
+  const uint32_t* w1;
+  int group;
+};
+
+struct MoeSmemLayout {
+  int ring;
+  int xs;
+  int xsum;
+  int sb;
+  int sb_stride;
+  int red;
+  int slots;
+  int fin;
+  int slot_tab;
+  int total;
+  int kslice;
+};
+
+// `C` = 256-column chunks of one item's K (stage 0: K/256; stage 1: T*K/256).
+__host__ __device__ inline MoeSmemLayout moe_smem_layout(int C, int gs, int cs, int stages) {
+  MoeSmemLayout L;
+  L.kslice = (C + cs - 1) / cs * kChunkCols;
+  int off = 1024;  // mbarriers; the ring starts 1024-aligned (128-byte swizzle)
+  L.ring = off;
+  off += kGemvWarps * stages * kMoeStageBytes;
+  L.xs = off;
+  off += L.kslice * 2;
+  L.xsum = off;
+  const int gsl = L.kslice / gs;
+  off += gsl * 4;
+  L.sb = off;
+  L.sb_stride = gsl | 1;
+  off += 32 * L.sb_stride * 4;
+  L.red = off;
+  off += 2 * kGemvWarps * 32 * 4;
+  L.slots = off;
+  if (cs > 1) off += 2 * cs * 32 * 4;
+  L.fin = off;
+  off += 32 * 4;
+  L.slot_tab = off;
+  off += kMoeMaxSlots * 8;
+  L.total = off + 1024;
+  return L;
+}
+
+// Local index of the expert of (token, slot) pair q, or -1 when it is not
+// resident.  Ids outside 0..e_total-1 set kDevErrBadIndex and are skipped.
+__device__ __forceinline__ int moe_local_expert(const MoeParams& p, int q) {
+  const int e = p.ids[q];
+  if (e < 0 || e >= p.e_total) {
+    record_device_error(kDevErrBadIndex);
+    return -1;
+  }
+  const int z = e - p.e_first;
+  return (z >= 0 && z < p.e_count) ? z : -1;
+}
+
+template <int STAGE, int GS>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    moe_affine_kernel(const MoeParams p, const __grid_constant__ CUtensorMap map0,
+                      const __grid_constant__ CUtensorMap map1) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  const int cs = p.cs;
+  const int S = p.stages;
+  const int cpe = p.K / kChunkCols;               // chunks per expert row
+  const int C = STAGE == 0 ? cpe : p.T * cpe;     // chunks per item
+  const int Kx = STAGE == 0 ? p.K : p.T * p.K;    // activation columns per token
+  const MoeSmemLayout L = moe_smem_layout(C, GS, cs, S);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int crank = cs > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int cluster = blockIdx.x / cs;
+  const int nclusters = gridDim.x / cs;
+  const int nitems = cluster < p.num_items ? (p.num_items - 1 - cluster) / nclusters + 1 : 0;
+  const int rgs = STAGE == 0 ? p.rows / 16 : p.rows / 32;  // items per pair (stage 0) / token
+
+  const int c0 = (C * crank) / cs;
+  const int cslice = (C * (crank + 1)) / cs - c0;
+  const int per_warp = (cslice + kGemvWarps - 1) / kGemvWarps;
+  const int wc0 = min(cslice, warp * per_warp);
+  const int mw = min(cslice, wc0 + per_warp) - wc0;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
+  uint8_t* ring = smem + L.ring + warp * (S * kMoeStageBytes);
+  uint8_t* xs = smem + L.xs;
+  float* xsum = reinterpret_cast<float*>(smem + L.xsum);
+  uint32_t* sb = reinterpret_cast<uint32_t*>(smem + L.sb);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* slots = reinterpret_cast<float*>(smem + L.slots);
+  float* fin = reinterpret_cast<float*>(smem + L.fin);
+  int* slot_z = reinterpret_cast<int*>(smem + L.slot_tab);
+  float* slot_w = reinterpret_cast<float*>(smem + L.slot_tab + kMoeMaxSlots * 4);
+  const uint32_t ring_a = smem_addr(ring) + lane * kMoeChunkBytes;
+  const uint64_t policy = l2_policy_evict_first();
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    if (warp == 0) {
+      prefetch_tensor_map(&map0);
+      if (STAGE == 0) prefetch_tensor_map(&map1);
+    }
+  }
+  __syncwarp();
+
+  // Expert ids (and, for stage 1, h) come from earlier kernels.
+  pdl_wait_primary();
+
+  // Producer cursor over this warp's tasks (item ordinal, warp-local chunk);
+  // tasks of non-resident experts are skipped identically by the consumer.
+  int p_ii = 0, p_j = 0, p_stage = 0;
+  auto seek = [&]() -> int {
+    while (p_ii < nitems) {
+      if (p_j >= mw) {
+        p_j = 0;
+        ++p_ii;
+        continue;
+      }
+      const int it = cluster + p_ii * nclusters;
+      const int z = STAGE == 0 ? moe_local_expert(p, it / rgs)
+                               : moe_local_expert(p, (it / rgs) * p.T + (c0 + wc0 + p_j) / cpe);
+      if (z >= 0) return z;
+      if (STAGE == 0) {
+        p_j = 0;
+        ++p_ii;
+      } else {
+        ++p_j;
+      }
+    }
+    return -1;
+  };
+  auto issue_next = [&]() -> bool {
+    const int z = seek();
+    if (z < 0) return false;
+    const int it = cluster + p_ii * nclusters;
+    const int chunk = c0 + wc0 + p_j;
+    if (lane == 0) {
+      uint8_t* dst = ring + p_stage * kMoeStageBytes;
+      mbar_arrive_expect_tx(&bars[p_stage], kMoeStageBytes);
+      if constexpr (STAGE == 0) {
+        const int row0 = (it % rgs) * 16;
+        tma_load_3d(dst, &map0, chunk * (kMoeChunkBytes / 8), row0, z, &bars[p_stage], policy);
+        tma_load_3d(dst + 16 * kMoeChunkBytes, &map1, chunk * (kMoeChunkBytes / 8), row0, z,
+                    &bars[p_stage], policy);
+      } else {
+        const int row0 = (it % rgs) * 32;
+        tma_load_3d(dst, &map0, (chunk % cpe) * (kMoeChunkBytes / 8), row0, z, &bars[p_stage], policy);
+      }
+    }
+    ++p_j;
+    if (++p_stage == S) p_stage = 0;
+    return true;
+  };
+
+  int issued = 0;
+  for (int t = 0; t < S; ++t) {
+    if (!issue_next()) break;
+    ++issued;
+  }
+  pdl_launch_dependents();
+
+  const int gsl = cslice * kChunkCols / GS;   // groups in this CTA's slice
+  const int gbase = c0 * (kChunkCols / GS);   // first of them, item-relative
+  const int G = p.K / GS;                     // groups per expert row
+  const int ld = L.kslice;
+  const uint32_t xs_a = smem_addr(xs);
+  const uint32_t xsum_a = smem_addr(xsum);
+  const uint32_t sb_a = smem_addr(sb) + lane * L.sb_stride * 4;
+
+  bool ok = true;
+  int fail_stage = 0, fail_pending = 0;
+  uint32_t fail_phase = 0;
+  int consumed = 0;
+  int stage = 0;
+  uint32_t phase = 0;
+  int done = 0;
+  int staged_tok = -1;
+
+  for (int ii = 0; ii < nitems; ++ii) {
+    const int it = cluster + ii * nclusters;
+    int tok, row0, pair = 0, zi = 0;
+    if constexpr (STAGE == 0) {
+      pair = it / rgs;
+      tok = pair / p.T;
+      row0 = (it % rgs) * 16;
+      zi = moe_local_expert(p, pair);
+      if (zi < 0) continue;  // uniform over the cluster
+    } else {
+      tok = it / rgs;
+      row0 = (it % rgs) * 32;
+    }
+    __syncthreads();  // the previous item's readers of xs / sb / slot tables are done
+    if (tok != staged_tok) {
+      stage_x_affine<GS>(p.x + (size_t)tok * Kx, xs, xsum, 1, 1, Kx, c0 * kChunkCols,
+                         cslice * kChunkCols, ld);
+      if constexpr (STAGE == 1) {
+        for (int t = threadIdx.x; t < p.T; t += blockDim.x) {
+          const int q = tok * p.T + t;
+          slot_z[t] = moe_local_expert(p, q);
+          slot_w[t] = __half2float(p.route[q]);
+        }
+      }
+      staged_tok = tok;
+    }
+    if constexpr (STAGE == 1) __syncthreads();  // slot_z is read below
+    for (int idx = threadIdx.x; idx < 32 * gsl; idx += blockDim.x) {
+      const int r = idx / gsl;
+      const int g = idx - r * gsl;
+      uint32_t v = 0;
+      if constexpr (STAGE == 0) {
+        const __half* sc = r < 16 ? p.s0 : p.s1;
+        const __half* bi = r < 16 ? p.b0 : p.b1;
+        const size_t gi = ((size_t)zi * p.rows + row0 + (r & 15)) * G + gbase + g;
+        v = (uint32_t)__half_as_ushort(sc[gi]) | ((uint32_t)__half_as_ushort(bi[gi]) << 16);
+      } else {
+        const int gg = gbase + g;          // group index over the token's T*K columns
+        const int t = gg / G;
+        const int z = slot_z[t];
+        if (z >= 0) {
+          const size_t gi = ((size_t)z * p.rows + row0 + r) * G + (gg - t * G);
+          v = (uint32_t)__half_as_ushort(p.s0[gi]) | ((uint32_t)__half_as_ushort(p.b0[gi]) << 16);
+        }
+      }
+      sb[r * L.sb_stride + g] = v;
+    }
+    __syncthreads();
+
+    float acc[1] = {0.f};
+    for (int j = 0; j < mw; ++j) {
+      const int cl = wc0 + j;  // slice-local chunk
+      float wt = 1.f;
+      if constexpr (STAGE == 1) {
+        const int t = (c0 + cl) / cpe;
+        if (slot_z[t] < 0) continue;
+        wt = slot_w[t];
+      }
+      if (ok && !mbar_wait(&bars[stage], phase)) {
+        ok = false;
+        fail_stage = stage;
+        fail_phase = phase;
+        fail_pending = issued - consumed;
+      }
+      ++consumed;
+      if (ok) {
+        const uint32_t src = ring_a + stage * kMoeStageBytes;
+        if constexpr (STAGE == 0) {
+          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), 0, xsum_a, 0, sb_a,
+                              cl * (kChunkCols / GS), acc);
+        } else {
+          float part[1] = {0.f};
+          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), 0, xsum_a, 0, sb_a,
+                              cl * (kChunkCols / GS), part);
+          acc[0] = fmaf(wt, part[0], acc[0]);
+        }
+      }
+      __syncwarp();
+      if (ok && issue_next()) ++issued;
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+
+    // Reduce the 4 warps, then the cs CTAs of the cluster, into fin[0..31].
+    float* rd = red + (done & 1) * (kGemvWarps * 32);
+    rd[warp * 32 + lane] = acc[0];
+    __syncthreads();
+    float* sl = slots + (done & 1) * (cs * 32);
+    if (threadIdx.x < 32) {
+      const int l = threadIdx.x;
+      const float v = (rd[l] + rd[32 + l]) + (rd[64 + l] + rd[96 + l]);
+      if (cs == 1) fin[l] = v;
+      else st_cluster_f32(map_to_rank(sl + crank * 32 + l, 0), v);
+    }
+    if (cs > 1) cluster_sync_all();
+    if (crank == 0) {
+      if (cs > 1 && threadIdx.x < 32) {
+        float v = 0.f;
+        for (int r = 0; r < cs; ++r) v += sl[r * 32 + threadIdx.x];
+        fin[threadIdx.x] = v;
+      }
+      __syncthreads();
+      if constexpr (STAGE == 0) {
+        if (threadIdx.x < 16) {
+          const int l = threadIdx.x;
+          const float g = __half2float(__float2half_rn(fin[l]));
+          const __half u = __float2half_rn(fin[16 + l]);
+          const __half sg = __float2half_rn(g / (1.0f + expf(-g)));
+          __half* h = static_cast<__half*>(p.out);
+          h[(size_t)pair * p.rows + row0 + l] = __float2half_rn(__half2float(sg) * __half2float(u));
+        }
+      } else {
+        if (threadIdx.x < 32) {
+          const size_t o = (size_t)tok * p.rows + row0 + threadIdx.x;
+          const float v = fin[threadIdx.x];
+          if (p.flags & kMoeOutF32) {
+            float* y = static_cast<float*>(p.out);
+            y[o] = (p.flags & kMoeAccumulate) ? y[o] + v : v;
+          } else {
+            __half* y = static_cast<__half*>(p.out);
+            y[o] = __float2half_rn((p.flags & kMoeAccumulate) ? __half2float(y[o]) + v : v);
+          }
+        }
+      }
+    }
+    ++done;
+  }
+
+  if (!ok) {
+    if (lane == 0) record_device_error(kDevErrBarrierTimeout);
+    uint32_t ph = fail_phase;
+    int sidx = fail_stage;
+    for (int j = 0; j < fail_pending; ++j) {
+      (void)mbar_wait(&bars[sidx], ph);
+      if (++sidx == S) {
+        sidx = 0;
+        ph ^= 1;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Generic kernels (any K % group == 0, group % 8 == 0, 4-byte aligned words):
+// one warp per output, plain loads.
+
+__device__ __forceinline__ float moe_row_dot(const uint32_t* w, const __half* s, const __half* b,
+                                             const __half* x, int K, int group, int lane) {
+  float acc = 0.f;
+  for (int wd = lane; wd < K / 8; wd += 32) {
+    const int g = (wd * 8) / group;
+    const float sc = __half2float(s[g]);
+    const float bi = __half2float(b[g]);
+    const uint32_t packed = w[wd];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) acc = fmaf(fmaf(float((packed >> (4 * n)) & 15u), sc, bi), __half2float(x[wd * 8 + n]), acc);
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  return acc;
+}
+
+// Stage 0: warp per (pair, row).
+__global__ void __launch_bounds__(256) moe_gate_up_generic_kernel(const MoeParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  if (gw >= (long long)p.ntok * p.T * p.rows) return;
+  const int pair = static_cast<int>(gw / p.rows);
+  const int row = static_cast<int>(gw - (long long)pair * p.rows);
+  const int z = moe_local_expert(p, pair);
+  if (z < 0) return;
+  const int G = p.K / p.group;
+  const size_t r = (size_t)z * p.rows + row;
+  const __half* x = p.x + (size_t)(pair / p.T) * p.K;
+  const float g = moe_row_dot(p.w0 + r * (p.K / 8), p.s0 + r * G, p.b0 + r * G, x, p.K, p.group, lane);
+  const float u = moe_row_dot(p.w1 + r * (p.K / 8), p.s1 + r * G, p.b1 + r * G, x, p.K, p.group, lane);
+  if (lane == 0) {
+    const float gh = __half2float(__float2half_rn(g));
+    const __half sg = __float2half_rn(gh / (1.0f + expf(-gh)));
+    static_cast<__half*>(p.out)[(size_t)pair * p.rows + row] =
+        __float2half_rn(__half2float(sg) * __half2float(__float2half_rn(u)));
+  }
+}
+
+// Stage 1: warp per (token, row).
+__global__ void __launch_bounds__(256) moe_down_generic_kernel(const MoeParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  if (gw >= (long long)p.ntok * p.rows) return;
+  const int tok = static_cast<int>(gw / p.rows);
+  const int row = static_cast<int>(gw - (long long)tok * p.rows);
+  const int G = p.K / p.group;
+  float acc = 0.f;
+  for (int t = 0; t < p.T; ++t) {
+    const int q = tok * p.T + t;
+    const int z = moe_local_expert(p, q);
+    if (z < 0) continue;
+    const size_t r = (size_t)z * p.rows + row;
+    const float d = moe_row_dot(p.w0 + r * (p.K / 8), p.s0 + r * G, p.b0 + r * G,
+                                p.x + (size_t)q * p.K, p.K, p.group, lane);
+    acc = fmaf(__half2float(p.route[q]), d, acc);
+  }
+  if (lane == 0) {
+    const size_t o = (size_t)tok * p.rows + row;
+    if (p.flags & kMoeOutF32) {
+      float* y = static_cast<float*>(p.out);
+      y[o] = (p.flags & kMoeAccumulate) ? y[o] + acc : acc;
+    } else {
+      __half* y = static_cast<__half*>(p.out);
+      y[o] = __float2half_rn((p.flags & kMoeAccumulate) ? __half2float(y[o]) + acc : acc);
+    }
+  }
+}
+
+}  // namespace gdsq

@@ -105,6 +105,43 @@ GDSQ_API int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, c
                               const void* x, void* y, int out_dim, int in_dim, int group_size,
                               int batch, void* stream);
 
+/* ---- Mixture-of-experts gather (affine-Q4 experts, decode) ------------- */
+
+/* No single reference launcher: these two calls replace the decode loop of
+ * moe_mlp_selective (gdsllm/runtime/qwen_moe.py:453-474), which per top-k slot
+ * reads the expert id to the host and calls launch_fused_affine_q4_gemv
+ * (affine_q4_dequant.h:41-44) three times with torch SiLU / mul / add between.
+ *
+ * Experts are stacked: *_weight [expert_count][rows][cols/8] uint32,
+ * *_scales / *_biases [expert_count][rows][cols/group_size] fp16, holding the
+ * experts expert_first .. expert_first+expert_count-1 of expert_total.
+ * expert_ids [num_tokens][top_k] int32 in device memory; slots whose expert is
+ * not resident are skipped (expert parallelism), ids outside 0..expert_total-1
+ * set device error bit 4 and are skipped.  top_k <= 64. */
+
+/* h[t][k][i] = fp16(silu(fp16(gate_e x_t)[i]) * fp16(up_e x_t)[i]), e = ids[t][k].
+ * gate/up rows = inter_dim, cols = hidden_dim; x [num_tokens][hidden_dim] fp16;
+ * h [num_tokens][top_k][inter_dim] fp16 (entries of non-resident slots are
+ * left unwritten). */
+GDSQ_API int gdsq_moe_affine_q4_gate_up(const void* gate_weight, const void* gate_scales,
+                                        const void* gate_biases, const void* up_weight,
+                                        const void* up_scales, const void* up_biases, const void* x,
+                                        const int32_t* expert_ids, void* h, int num_tokens, int top_k,
+                                        int inter_dim, int hidden_dim, int group_size, int expert_first,
+                                        int expert_count, int expert_total, void* stream);
+
+#define GDSQ_MOE_OUT_F32 1    /* y is fp32 instead of fp16 */
+#define GDSQ_MOE_ACCUMULATE 2 /* y += result instead of y = result */
+
+/* y[t][j] = sum over resident slots k of route_weights[t][k] * (down_e h[t][k])[j],
+ * summed in fp32.  down rows = hidden_dim, cols = inter_dim; route_weights
+ * [num_tokens][top_k] fp16; y [num_tokens][hidden_dim]. */
+GDSQ_API int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales,
+                                     const void* down_biases, const void* h, const int32_t* expert_ids,
+                                     const void* route_weights, void* y, int num_tokens, int top_k,
+                                     int hidden_dim, int inter_dim, int group_size, int expert_first,
+                                     int expert_count, int expert_total, int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -111,3 +111,32 @@ def test_gemv_cpu_path_is_within_the_bar():
     y = oracle.gemv_cpu(w, x)
     err = np.abs(y.astype(np.float64) - oracle.gemv_exact(w, x))
     assert (err <= oracle.error_bound(w, x)[:, None]).all()
+
+
+def test_moe_oracle_matches_reference_decode_code():
+    """oracle.moe_mlp_reference reproduces, bit for bit, GdsLLM's own
+    moe_mlp_selective decode arithmetic (recorded by make_moe_golden.py with
+    the fused GEMV replaced by the oracle's CPU GEMV)."""
+    z = np.load(GOLDEN / "moe_decode.npz")
+    g = int(z["group"])
+
+    def st(name):
+        return (z[f"{name}_w"], z[f"{name}_s"], z[f"{name}_b"])
+
+    y = oracle.moe_mlp_reference(z["x"], z["ids"], z["route_w"], st("gate"), st("up"), st("down"), g,
+                                 shared=(st("sgate"), st("sup"), st("sdown")),
+                                 shared_gate_w=z["shared_gate_w"])
+    assert_f16_bitexact(y, z["y"], "moe decode")
+
+
+def test_moe_exact_forms_agree_with_reference_sequence():
+    """The fp64 stage forms used as GPU bars stay within their own bars of
+    the reference's fp16 sequence (a check of the bars, on the fixture)."""
+    z = np.load(GOLDEN / "moe_decode.npz")
+    g = int(z["group"])
+    gate, up, down = [(z[f"{n}_w"], z[f"{n}_s"], z[f"{n}_b"]) for n in ("gate", "up", "down")]
+    h, _, _ = oracle.moe_gate_up_exact(z["x"], z["ids"], gate, up, g)
+    y, bar = oracle.moe_down_exact(h, z["ids"], z["route_w"], down, g)
+    ref = oracle.moe_decode_reference(z["x"], z["ids"], z["route_w"], gate, up, down, g)
+    err = np.abs(y - ref.astype(np.float64))
+    assert (err <= 4 * bar[:, None] + 16 * 2.0 ** -10 * np.abs(ref.astype(np.float64)) + 1e-6).all()
