@@ -19,6 +19,7 @@
 #include "dequant.cuh"
 #include "gemv.cuh"
 #include "gemv_tc.cuh"
+#include "gemv_tcb.cuh"
 #include "moe.cuh"
 
 namespace gdsq {
@@ -334,8 +335,10 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
   const uint64_t key = ((uint64_t)F << 60) | ((uint64_t)B << 54) | ((uint64_t)GS << 44) |
                        ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
   GemvPlan plan;
+  int ocs, ost, ocp;
+  const bool forced = plan_override(&ocs, &ost, &ocp);  // tuning runs: plan afresh, do not cache
   bool have = false;
-  {
+  if (!forced) {
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans[dev.ordinal].find(key);
     if (it != g_plans[dev.ordinal].end()) {
@@ -346,8 +349,10 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
   if (!have) {
     int st = make_plan<F, B, GS>(p.N, p.K, dev, &plan);
     if (st != GDSQ_OK) return st;
-    std::lock_guard<std::mutex> lock(g_plan_mutex);
-    g_plans[dev.ordinal][key] = plan;
+    if (!forced) {
+      std::lock_guard<std::mutex> lock(g_plan_mutex);
+      g_plans[dev.ordinal][key] = plan;
+    }
   }
   CUtensorMap wmap;
   int mst = weight_map<F>(dev, p.w, p.N, p.row_bytes, &wmap);
@@ -489,6 +494,129 @@ int launch_tc_q4_0(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
   return GDSQ_OK;
 }
 
+// Tensor-core batched GEMV (gemv_tcb.cuh): default for batch >= 5, where
+// the CUDA-core kernel's multiply-add work (linear in the batch) outgrows
+// the tensor-core kernel's fixed dequantization cost; GDSQ_GEMV_TCB=0 turns
+// it off, =1 uses it for every batch size.
+int tcb_mode() {
+  const char* e = getenv("GDSQ_GEMV_TCB");
+  if (!e || !*e) return -1;
+  return e[0] == '1' ? 1 : 0;
+}
+
+// One CTA per SM.  Cost = the busiest CTA's chunks (plus two chunks' worth
+// of fixed cost per row tile: pipeline fill, epilogue, cluster reduction),
+// with a small penalty per cluster doubling.
+template <int F, int B, int GS>
+int make_tcb_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
+  auto kernel = gemv_tcb_kernel<F, B, GS>;
+  const int R = (N + kTbRows - 1) / kTbRows;
+  const int C = K / kChunkCols;
+  int force_cs = 0, force_st = 0, force_cp = 0;
+  const bool forced = plan_override(&force_cs, &force_st, &force_cp);
+  double best = 1e30;
+  bool found = false;
+  for (int cs = 1; cs <= kTbMaxCluster; cs *= 2) {
+    if (cs > C || cs > dev.sms) break;
+    if (forced && cs != force_cs) continue;
+    const int cslice = (C + cs - 1) / cs;
+    for (int st = 3; st <= kTbMaxStages; ++st) {
+      if (forced && st != force_st) continue;
+      const TbLayout L = tb_layout<F, B>(cs, st);
+      if (L.total > dev.smem_optin) continue;
+      const int nclusters = (int)((long long)R * cs <= dev.sms ? R : dev.sms / cs);
+      const int items = (R + nclusters - 1) / nclusters;
+      const double cost = (double)items * (cslice + 2) * (1.0 + 0.04 * (cs > 1) + 0.02 * (cs > 2) + 0.02 * (cs > 4)) *
+                          (1.0 - 0.01 * st);
+      if (cost < best) {
+        best = cost;
+        found = true;
+        out->cs = cs;
+        out->stages = st;
+        out->copy = 1;
+        out->nclusters = nclusters;
+        out->smem = L.total;
+      }
+    }
+  }
+  if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no tensor-core GEMV plan fits shared memory");
+  cudaError_t e = ensure_smem(kernel, out->smem, dev.ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tcb)");
+  return GDSQ_OK;
+}
+
+template <int F, int B, int GS>
+int launch_tcb(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
+  const uint64_t key = ((uint64_t)3 << 62) | ((uint64_t)F << 58) | ((uint64_t)B << 52) | ((uint64_t)GS << 42) |
+                       ((uint64_t)(unsigned)p.N << 20) | (uint64_t)(unsigned)(p.K / 32);
+  GemvPlan plan;
+  int ocs, ost, ocp;
+  const bool forced = plan_override(&ocs, &ost, &ocp);  // tuning runs: plan afresh, do not cache
+  bool have = false;
+  if (!forced) {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = g_plans[dev.ordinal].find(key);
+    if (it != g_plans[dev.ordinal].end()) {
+      plan = it->second;
+      have = true;
+    }
+  }
+  if (!have) {
+    int st = make_tcb_plan<F, B, GS>(p.N, p.K, dev, &plan);
+    if (st != GDSQ_OK) return st;
+    if (!forced) {
+      std::lock_guard<std::mutex> lock(g_plan_mutex);
+      g_plans[dev.ordinal][key] = plan;
+    }
+  }
+  CUtensorMap wmap;
+  int mst = weight_map<F>(dev, p.w, p.N, p.row_bytes, &wmap, kTbRows);
+  if (mst != GDSQ_OK) return mst;
+  auto kernel = gemv_tcb_kernel<F, B, GS>;
+  cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tcb)");
+  p.cs = plan.cs;
+  p.stages = plan.stages;
+  p.copy = 1;
+  p.num_rg = (p.N + kTbRows - 1) / kTbRows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.nclusters * plan.cs);
+  cfg.blockDim = dim3(kTbThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (plan.cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = plan.cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g_pdl_enabled) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv tcb launch");
+  return GDSQ_OK;
+}
+
+template <int F, int GS>
+int launch_tcb_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t stream) {
+  switch (batch_tile(p.nb)) {
+    case 1: return launch_tcb<F, 1, GS>(p, dev, stream);
+    case 2: return launch_tcb<F, 2, GS>(p, dev, stream);
+    case 3: return launch_tcb<F, 3, GS>(p, dev, stream);
+    case 4: return launch_tcb<F, 4, GS>(p, dev, stream);
+    case 8: return launch_tcb<F, 8, GS>(p, dev, stream);
+    default: return launch_tcb<F, 16, GS>(p, dev, stream);
+  }
+}
+
 template <int F>
 int launch_generic(const GemvParams& p, cudaStream_t stream) {
   const dim3 grid((p.N + 7) / 8);
@@ -565,6 +693,19 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
                                  : (long long)in_dim / 2;
 
   const bool shape_ok = in_dim % kChunkCols == 0 && aligned(w, 16) && aligned(x, 16);
+  const int tcb = tcb_mode();
+  const bool use_tcb = shape_ok && (tcb == 1 || (tcb == -1 && batch >= 5));
+  if (use_tcb) {
+    if (fmt == kFmtQ4_0) return launch_tcb_batch<kFmtQ4_0, 0>(p, *dev, stream);
+    if (fmt == kFmtQ8_0) return launch_tcb_batch<kFmtQ8_0, 0>(p, *dev, stream);
+    switch (group) {
+      case 32: return launch_tcb_batch<kFmtAffineQ4, 32>(p, *dev, stream);
+      case 64: return launch_tcb_batch<kFmtAffineQ4, 64>(p, *dev, stream);
+      case 128: return launch_tcb_batch<kFmtAffineQ4, 128>(p, *dev, stream);
+      case 256: return launch_tcb_batch<kFmtAffineQ4, 256>(p, *dev, stream);
+      default: break;  // other group sizes: CUDA-core kernels below
+    }
+  }
   if (fmt == kFmtQ4_0) {
     if (shape_ok && batch == 1 && tc_enabled()) return launch_tc_q4_0(p, *dev, stream);
     if (shape_ok && fast_min_smem<kFmtQ4_0>(batch, in_dim, 0) <= dev->smem_optin)

@@ -222,3 +222,70 @@ def test_gemv_q4_0_tensor_core_kernel(gdsq, cuda, n, k, monkeypatch):
     y = gdsq.gemv_q4_0(w.to(cuda), x, n, k)
     torch.cuda.synchronize()
     _check_gemv(y, oracle.dequant_q4_0(w.numpy()).reshape(n, k), x, f"q4_0 tc {n}x{k}")
+
+
+# ---- tensor-core batched GEMV (default for batch >= 2) ----------------------
+
+def _weights(fmt, n, k, g, seed):
+    if fmt == "q4_0":
+        w = synth.q4_0_weight(n, k, seed=seed)
+        return (w,), oracle.dequant_q4_0(w.numpy()).reshape(n, k)
+    if fmt == "q8_0":
+        w = synth.q8_0_weight(n, k, seed=seed)
+        return (w,), oracle.dequant_q8_0(w.numpy()).reshape(n, k)
+    words, s, b = synth.affine_q4_weight(n, k, group=g, seed=seed)
+    return (words, s, b), oracle.dequant_affine_q4(words.numpy(), s.numpy(), b.numpy(), g).reshape(n, k)
+
+
+def _run(gdsq, fmt, ws, x, n, k, g):
+    ws = [t.to(x.device) for t in ws]
+    if fmt == "q4_0":
+        return gdsq.gemv_q4_0(ws[0], x, n, k)
+    if fmt == "q8_0":
+        return gdsq.gemv_q8_0(ws[0], x, n, k)
+    return gdsq.gemv_affine_q4(ws[0], ws[1], ws[2], x, n, k, g)
+
+
+@pytest.mark.parametrize("fmt,g", [("q4_0", 0), ("q8_0", 0), ("affine", 128), ("affine", 32), ("affine", 256)])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (11008, 4096), (4096, 11008), (300, 1024), (129, 512)])
+@pytest.mark.parametrize("batch", [1, 2, 5, 8, 16])
+def test_gemv_tensor_core_batched(gdsq, cuda, fmt, g, n, k, batch, monkeypatch):
+    """The tcgen05 batched kernel (forced on for batch 1 as well) meets the
+    GEMV bar for every format, odd row counts and every batch tile."""
+    monkeypatch.setenv("GDSQ_GEMV_TCB", "1")
+    ws, w16 = _weights(fmt, n, k, g, seed=n + batch)
+    x = synth.activations(batch, k, seed=k + batch).to(cuda)
+    y = _run(gdsq, fmt, ws, x, n, k, g)
+    torch.cuda.synchronize()
+    _check_gemv(y, w16, x, f"tcb {fmt} g{g} {n}x{k} b{batch}")
+
+
+@pytest.mark.parametrize("plan", ["1:3", "1:5", "2:3", "2:4", "4:3", "8:3"])
+@pytest.mark.parametrize("fmt,g", [("q4_0", 0), ("q8_0", 0), ("affine", 64)])
+def test_gemv_tensor_core_launch_plans(gdsq, cuda, fmt, g, plan, monkeypatch):
+    """Every cluster split and ring depth of the tensor-core kernel, including
+    K slices of uneven length and several row tiles per cluster."""
+    monkeypatch.setenv("GDSQ_GEMV_TCB", "1")
+    monkeypatch.setenv("GDSQ_GEMV_PLAN", plan)
+    n, k, batch = 1000, 2560, 6
+    ws, w16 = _weights(fmt, n, k, g, seed=3)
+    x = synth.activations(batch, k, seed=4).to(cuda)
+    y = _run(gdsq, fmt, ws, x, n, k, g)
+    torch.cuda.synchronize()
+    _check_gemv(y, w16, x, f"tcb plan {plan} {fmt}")
+    assert gdsq.device_error(0, clear=True) == 0
+
+
+def test_gemv_batched_paths_agree(gdsq, cuda, monkeypatch):
+    """Tensor-core and CUDA-core batched results are both within the bar of
+    the exact product (and so within twice the bar of each other)."""
+    n, k, batch = 4096, 4096, 8
+    ws, w16 = _weights("q4_0", n, k, 0, seed=12)
+    x = synth.activations(batch, k, seed=13).to(cuda)
+    monkeypatch.setenv("GDSQ_GEMV_TCB", "0")
+    y_cc = _run(gdsq, "q4_0", ws, x, n, k, 0)
+    monkeypatch.setenv("GDSQ_GEMV_TCB", "1")
+    y_tc = _run(gdsq, "q4_0", ws, x, n, k, 0)
+    torch.cuda.synchronize()
+    _check_gemv(y_cc, w16, x, "cuda cores")
+    _check_gemv(y_tc, w16, x, "tensor cores")
