@@ -415,6 +415,16 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
+// Split form: an early relaxed arrive only announces "this CTA is running";
+// the matching wait, just before the first distributed-shared-memory store,
+// then costs nothing when every peer started long ago.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Address of `local` (a shared::cta address in this CTA's window) in the
 // shared memory of cluster CTA `rank`.
 __device__ __forceinline__ uint32_t map_to_rank(const void* local, uint32_t rank) {
@@ -476,6 +486,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     if (warp == 0) prefetch_tensor_map(&wmap);
   }
   __syncwarp();
+  if (cs > 1) cluster_arrive_relaxed();  // waited for before the first DSMEM store
 
   // Producer cursor: the next (item, step) to copy and the stage it goes to.
   int p_item = 0, p_step = 0, p_stage = 0, issued = 0;
@@ -524,7 +535,6 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   else stage_x_affine<GS>(p.x, xs, xsum, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
-  if (cs > 1) cluster_sync_all();  // every CTA of the cluster is running before any DSMEM write
   __syncthreads();
 
   const uint32_t xs_a = smem_addr(xs);
@@ -589,6 +599,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     float* rd = red + (item & 1) * (kGemvWarps * B * 32);
 #pragma unroll
     for (int b = 0; b < B; ++b) rd[(warp * B + b) * 32 + lane] = acc[b];
+    if (cs > 1 && item == 0) cluster_wait();  // every peer is running: DSMEM stores are safe
     __syncthreads();
     float* sl = slots + (item & 1) * (cs * B * 32);
     for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {
@@ -619,6 +630,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     }
   }
 
+  if (cs > 1 && nitems == 0) cluster_wait();  // pairs the early arrive
   if (!ok) {
     // A copy never completed.  Record it and wait (bounded) for the copies
     // still in flight into this warp's ring (at most S, starting with the one

@@ -172,6 +172,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     }
   }
   __syncwarp();
+  if (cs > 1) cluster_arrive_relaxed();  // waited for before the first DSMEM store
+  bool peers_waited = false;
 
   // Expert ids (and, for stage 1, h) come from earlier kernels.
   pdl_wait_primary();
@@ -334,6 +336,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     // Reduce the 4 warps, then the cs CTAs of the cluster, into fin[0..31].
     float* rd = red + (done & 1) * (kGemvWarps * 32);
     rd[warp * 32 + lane] = acc[0];
+    if (cs > 1 && !peers_waited) {
+      cluster_wait();  // every peer is running: DSMEM stores are safe
+      peers_waited = true;
+    }
     __syncthreads();
     float* sl = slots + (done & 1) * (cs * 32);
     if (threadIdx.x < 32) {
@@ -376,6 +382,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     ++done;
   }
 
+  if (cs > 1 && !peers_waited) cluster_wait();  // pairs the early arrive
   if (!ok) {
     if (lane == 0) record_device_error(kDevErrBarrierTimeout);
     uint32_t ph = fail_phase;
