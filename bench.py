@@ -26,6 +26,8 @@ as ``ref_cuda``.
 --gpus N (under torchrun): N independent replicas (weak scaling).
 --config 0: one 11008x4096 Q4_0 GEMV, rotating over copies larger than L2.
 --config 2: Q8_0 / affine-Q4 sweep (4 shapes x batch 1, 4, 8, 16).
+--config 3: LLaMA-70B-shaped decode chain, tensor-parallel over --gpus N (NCCL all-reduce).
+--config 4: Qwen-MoE-shaped MoE decode, expert-parallel over --gpus N (--batch 1 or 8).
 """
 from __future__ import annotations
 
@@ -597,13 +599,163 @@ def bench_config2(args, dist):
             "sweep": points, "gpu_launches": launches}
 
 
+def bench_config3(args, dist):
+    """LLaMA-70B-shaped Q4_0 decode GEMV chain, tensor-parallel over the ranks
+    per layer q, k, v, gate, up column-split, o and down
+    row-split with one NCCL all-reduce each; Q8_0 lm_head column-split with an
+    all-gather of the logits.  Every rank holds only its shards (38.5 GB / N).
+    One step = one token through all 80 layers; captured as one CUDA graph."""
+    from gdsllm_b200 import capi, lib as gdsq_lib
+    import torch.distributed as tdist
+    peak, peak_kind = load_peaks()
+    lib = gdsq_lib()
+    capi.set_pdl(bool(args.pdl))
+    H, Q, KV, FF, V, NL = 8192, 8192, 1024, 28672, 32000, 80
+    ws, rank, dev = dist.world, dist.rank, dist.device
+    cols = {"q": (Q // ws, H), "k": (KV // ws, H), "v": (KV // ws, H), "gate": (FF // ws, H), "up": (FF // ws, H)}
+    rows = {"o": (H, Q // ws), "down": (H, FF // ws)}
+    layers = []
+    for layer in range(NL):
+        wl = {}
+        for j, (name, (n, k)) in enumerate(list(cols.items()) + list(rows.items())):
+            wl[name] = synth.q4_0_weight(n, k, seed=(layer * 16 + j) * 64 + rank, device=dev)
+        layers.append(wl)
+    lm = synth.q8_0_weight(V // ws, H, seed=999 * 64 + rank, device=dev)
+    x0 = synth.activations(1, H, seed=5, device=dev)
+    buf = {name: torch.empty(1, n, dtype=torch.float16, device=dev) for name, (n, _) in cols.items()}
+    o_out = torch.empty(1, H, dtype=torch.float16, device=dev)
+    d_out = torch.empty(1, H, dtype=torch.float16, device=dev)
+    logits_local = torch.empty(1, V // ws, dtype=torch.float16, device=dev)
+    logits = torch.empty(ws, V // ws, dtype=torch.float16, device=dev)
+    wbytes_rank = sum(t.numel() for wl in layers for t in wl.values()) + lm.numel()
+
+    def gemv(fmt, w, x, y, n, k, stream):
+        fn = lib.gdsq_fused_q4_0_gemv if fmt == "q4_0" else lib.gdsq_fused_q8_0_gemv
+        st = fn(w.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, 1, stream)
+        if st:
+            raise RuntimeError(lib.gdsq_last_error().decode())
+
+    def token(stream):
+        x = x0
+        for wl in layers:
+            for name, (n, k) in cols.items():
+                if name in ("q", "k", "v"):
+                    gemv("q4_0", wl[name], x, buf[name], n, k, stream)
+            gemv("q4_0", wl["o"], buf["q"], o_out, H, Q // ws, stream)   # attention output stands in as q's shard
+            if ws > 1:
+                tdist.all_reduce(o_out)
+            gemv("q4_0", wl["gate"], o_out, buf["gate"], FF // ws, H, stream)
+            gemv("q4_0", wl["up"], o_out, buf["up"], FF // ws, H, stream)
+            gemv("q4_0", wl["down"], buf["up"], d_out, H, FF // ws, stream)
+            if ws > 1:
+                tdist.all_reduce(d_out)
+            x = d_out
+        gemv("q8_0", lm, x, logits_local, V // ws, H, stream)
+        if ws > 1:
+            tdist.all_gather_into_tensor(logits, logits_local)
+
+    if ws > 1:  # NCCL communicators exist before capture
+        tdist.all_reduce(o_out)
+        tdist.all_gather_into_tensor(logits, logits_local)
+        torch.cuda.synchronize()
+    g = capture(token)
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dev) if rank == 0 else None)
+    del g
+    tok_s = args.steps / (ms / 1e3)
+    per_token_bytes = wbytes_rank * ws
+    launches = args.steps * (NL * 7 + 1)
+    return {"metric": "LLaMA-70B-shaped Q4_0 batch-1 decode tok/s, tensor-parallel GEMV chain (560 Q4_0 "
+                      "projections + Q8_0 lm_head per token, NCCL all-reduce after o and down)",
+            "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random Q4_0/Q8_0 shards, config 3 shapes)",
+            "config": {"workload": "config 3: 80 layers, hidden 8192, q 8192 / kv 1024 rows, FFN 28672, vocab 32000 "
+                                   "(Q8_0 lm_head), batch 1; attention and norms are not on the path",
+                       "parallelism": f"tp{ws}", "weights_per_gpu_gb": round(wbytes_rank / 1e9, 2),
+                       "l2": "every token streams 38.5 GB / N per GPU (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(wbytes_rank / (ms / args.steps / 1e3) / 1e9, 1),
+                         "peak": peak, "unit": "GB/s",
+                         "frac": round(wbytes_rank / (ms / args.steps / 1e3) / 1e9 / peak, 4),
+                         "peak_kind": peak_kind, "scope": "per-GPU weight bytes / token time (whole step)"},
+            "aggregate_weight_gbs": round(per_token_bytes * tok_s / 1e9, 1),
+            "gpu_launches": launches, "clocks": clk}
+
+
+def bench_config4(args, dist):
+    """Qwen-MoE-shaped affine-Q4 MoE decode, expert-parallel over the ranks
+    60 MoE layers (8 distinct resident layers cycled),
+    512 experts + 1 shared (hidden 4096, intermediate 1024), fp16 router with
+    top-10; experts split 512 / N per GPU, one NCCL all-reduce of the fp32
+    partial sums per layer.  One step = one decode step of `--batch` tokens."""
+    from gdsllm_b200 import capi, ep, moe
+    peak, peak_kind = load_peaks()
+    capi.set_pdl(bool(args.pdl))
+    E, H, I, G, TOPK, NL, NPHYS = 512, 4096, 1024, 128, 10, 60, 8
+    ws, rank, dev = dist.world, dist.rank, dist.device
+    B = args.batch
+    first, count = ep.expert_range(rank, ws, E)
+    gen = torch.Generator().manual_seed(1)
+    layers = []
+    for l in range(NPHYS):
+        def st(rows, cols, seed, e):
+            return synth.affine_q4_weight(rows, cols, group=G, seed=seed, device=dev, lead=(e,))
+        base = (l * 8) * 64
+        router = (torch.randn(E, H, generator=gen) / H ** 0.5).half().to(dev)
+        sgate = (torch.randn(1, H, generator=gen) / H ** 0.5).half().to(dev)
+        layers.append(moe.MoeLayer(
+            router=router, gate=st(I, H, base + 1 + rank * 8, count), up=st(I, H, base + 2 + rank * 8, count),
+            down=st(H, I, base + 3 + rank * 8, count), group=G, expert_first=first, expert_total=E,
+            shared=(st(I, H, base + 4, 1), st(I, H, base + 5, 1), st(H, I, base + 6, 1)), shared_gate=sgate))
+    mods = [ep.ExpertParallelMoE(layer, top_k=TOPK) for layer in layers] if ws > 1 else None
+    x0 = synth.activations(B, H, seed=3, device=dev)
+
+    def step(stream):
+        x = x0
+        for l in range(NL):
+            layer = layers[l % NPHYS]
+            y = mods[l % NPHYS](x) if ws > 1 else moe.moe_mlp_decode(x, layer, TOPK)
+            x = x + y
+        return x
+
+    # bytes touched per step (whole job): routing of an eager pass
+    touched = 0
+    x = x0
+    with torch.no_grad():
+        for l in range(NL):
+            layer = layers[l % NPHYS]
+            ids = moe.route(x, layer.router, TOPK)[0]
+            distinct = int(torch.unique(ids).numel())
+            touched += E * H * 2 + (distinct + 1) * 3 * (I * H // 2 + 2 * 2 * I * H // G)
+            x = x + (mods[l % NPHYS](x) if ws > 1 else moe.moe_mlp_decode(x, layer, TOPK))
+    torch.cuda.synchronize()
+    g = capture(step)
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dev) if rank == 0 else None)
+    del g
+    step_s = ms / args.steps / 1e3
+    return {"metric": "Qwen-MoE-shaped affine-Q4 MoE decode tok/s, expert-parallel (60 layers x (router top-10 + "
+                      "fused expert gather + shared expert), NCCL all-reduce per layer)",
+            "value": round(B / step_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random affine-Q4 experts, config 4 shapes)",
+            "config": {"workload": f"config 4: 512 experts + shared, hidden 4096, expert intermediate 1024, top-10, "
+                                   f"batch {B}, 60 layers cycling {NPHYS} resident layers",
+                       "parallelism": f"ep{ws}", "experts_per_gpu": count,
+                       "touched_weight_gb_per_step": round(touched / 1e9, 3),
+                       "l2": f"{NPHYS} resident layers of {E * 3 * 2.23 / 1e3:.1f} GB each (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(touched / ws / step_s / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(touched / ws / step_s / 1e9 / peak, 4), "peak_kind": peak_kind,
+                         "scope": "touched weight bytes per GPU / step time (whole step)"},
+            "gpu_launches": args.steps * NL * (4 + 4), "clocks": clk}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2])
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--batch", type=int, default=1, help="config 4: tokens per decode step (1 or 8)")
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
@@ -617,6 +769,10 @@ def main():
             res = bench_config0(args, dist)
         elif args.config == 2:
             res = bench_config2(args, dist)
+        elif args.config == 3:
+            res = bench_config3(args, dist)
+        elif args.config == 4:
+            res = bench_config4(args, dist)
         else:
             res = bench_ours(args, dist)
         if dist.rank == 0 and res is not None:

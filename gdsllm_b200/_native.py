@@ -30,10 +30,13 @@ _C_SIGNATURES = {
                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                  ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  ctypes.c_void_p]),
-    "gdsq_moe_affine_q4_gate_up": (ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int] * 8
+    "gdsq_moe_affine_q4_gate_up": (ctypes.c_int, [ctypes.c_void_p] * 15 + [ctypes.c_int] * 8
                                    + [ctypes.c_void_p]),
-    "gdsq_moe_affine_q4_down": (ctypes.c_int, [ctypes.c_void_p] * 7 + [ctypes.c_int] * 9
+    "gdsq_moe_affine_q4_down": (ctypes.c_int, [ctypes.c_void_p] * 11 + [ctypes.c_int] * 9
                                 + [ctypes.c_void_p]),
+    "gdsq_moe_route": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p]),
 }
 
 

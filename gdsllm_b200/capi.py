@@ -84,31 +84,39 @@ def gemv_affine_q4(words, scales, biases, x: torch.Tensor, n: int, k: int, group
 
 MOE_OUT_F32 = 1      # GDSQ_MOE_OUT_F32
 MOE_ACCUMULATE = 2   # GDSQ_MOE_ACCUMULATE
+MOE_CLAMP = 4        # GDSQ_MOE_CLAMP
+
+
+def _shared_ptrs(shared, n):
+    if shared is None:
+        return [None] * n
+    return [t.data_ptr() for m in shared for t in m]
 
 
 def moe_gate_up(gate, up, x: torch.Tensor, ids: torch.Tensor, group: int, expert_first: int = 0,
-                expert_total: int | None = None, out=None) -> torch.Tensor:
-    """h [ntok, top_k, inter] = fp16(silu(gate_e x) * up_e x) for e = ids.
+                expert_total: int | None = None, out=None, shared=None) -> torch.Tensor:
+    """h [ntok, top_k (+1 with shared), inter] = fp16(silu(gate_e x) * up_e x).
     gate / up: (words int32 [E, inter, hidden/8], scales, biases); ids int32
-    [ntok, top_k]."""
+    [ntok, top_k]; shared = (shared gate stack, shared up stack) with E = 1."""
     gw, gs, gb = gate
     uw, us, ub = up
     e, inter, hidden = gw.shape[0], gw.shape[1], gw.shape[2] * 8
     ntok, top_k = ids.shape
     total = expert_first + e if expert_total is None else expert_total
     if out is None:
-        out = torch.empty((ntok, top_k, inter), dtype=torch.float16, device=x.device)
-    check(lib().gdsq_moe_affine_q4_gate_up(_p(gw), _p(gs), _p(gb), _p(uw), _p(us), _p(ub), _p(x), _p(ids),
-                                           _p(out), ntok, top_k, inter, hidden, group, expert_first, e,
-                                           total, _stream(x)), "gdsq_moe_affine_q4_gate_up")
+        out = torch.empty((ntok, top_k + (shared is not None), inter), dtype=torch.float16, device=x.device)
+    check(lib().gdsq_moe_affine_q4_gate_up(_p(gw), _p(gs), _p(gb), _p(uw), _p(us), _p(ub), *_shared_ptrs(shared, 6),
+                                           _p(x), _p(ids), _p(out), ntok, top_k, inter, hidden, group, expert_first,
+                                           e, total, _stream(x)), "gdsq_moe_affine_q4_gate_up")
     return out
 
 
 def moe_down(down, h: torch.Tensor, ids: torch.Tensor, route: torch.Tensor, group: int,
-             expert_first: int = 0, expert_total: int | None = None, out=None, flags: int = 0) -> torch.Tensor:
-    """y [ntok, hidden] = sum_k route[:, k] * down_e h[:, k] (fp32 sum).
-    down: (words int32 [E, hidden, inter/8], scales, biases); route fp16
-    [ntok, top_k]."""
+             expert_first: int = 0, expert_total: int | None = None, out=None, flags: int = 0,
+             shared=None, shared_weights=None) -> torch.Tensor:
+    """y [ntok, hidden] = sum_k route[:, k] * down_e h[:, k] (+ shared_weights *
+    shared_down h[:, top_k]) in fp32.  down: (words int32 [E, hidden, inter/8],
+    scales, biases); route fp16 [ntok, top_k]; shared = the shared down stack."""
     dw, ds, db = down
     e, hidden, inter = dw.shape[0], dw.shape[1], dw.shape[2] * 8
     ntok, top_k = ids.shape
@@ -116,7 +124,23 @@ def moe_down(down, h: torch.Tensor, ids: torch.Tensor, route: torch.Tensor, grou
     if out is None:
         dt = torch.float32 if flags & MOE_OUT_F32 else torch.float16
         out = torch.empty((ntok, hidden), dtype=dt, device=h.device)
-    check(lib().gdsq_moe_affine_q4_down(_p(dw), _p(ds), _p(db), _p(h), _p(ids), _p(route), _p(out), ntok,
-                                        top_k, hidden, inter, group, expert_first, e, total, flags,
-                                        _stream(h)), "gdsq_moe_affine_q4_down")
+    sh = [None] * 3 if shared is None else [t.data_ptr() for t in shared]
+    check(lib().gdsq_moe_affine_q4_down(_p(dw), _p(ds), _p(db), *sh, _p(h), _p(ids), _p(route),
+                                        _p(shared_weights), _p(out), ntok, top_k, hidden, inter, group,
+                                        expert_first, e, total, flags, _stream(h)), "gdsq_moe_affine_q4_down")
     return out
+
+
+def moe_route(logits: torch.Tensor, top_k: int, x: torch.Tensor | None = None,
+              shared_gate: torch.Tensor | None = None):
+    """(ids int32 [ntok, k], weights fp16 [ntok, k], shared weight fp16 [ntok] or
+    None) from router logits fp16 [ntok, E] -- moe_route's top-k / softmax
+    tail, plus sigmoid(x . shared_gate)."""
+    ntok, e = logits.shape
+    ids = torch.empty(ntok, top_k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(ntok, top_k, dtype=torch.float16, device=logits.device)
+    sw = None if shared_gate is None else torch.empty(ntok, dtype=torch.float16, device=logits.device)
+    hidden = 0 if x is None else x.shape[-1]
+    check(lib().gdsq_moe_route(_p(logits), ntok, e, top_k, _p(x), _p(shared_gate), hidden, _p(ids), _p(w), _p(sw),
+                               _stream(logits)), "gdsq_moe_route")
+    return ids, w, sw

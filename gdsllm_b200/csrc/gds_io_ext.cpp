@@ -522,7 +522,8 @@ torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, 
                                      ExpertStack gate, ExpertStack up, ExpertStack down, int group_size,
                                      int64_t expert_first, int64_t expert_total,
                                      c10::optional<torch::Tensor> out, bool accumulate, bool out_fp32,
-                                     c10::optional<torch::Tensor> h) {
+                                     c10::optional<torch::Tensor> h, c10::optional<std::vector<torch::Tensor>> shared,
+                                     c10::optional<torch::Tensor> shared_weights, bool clamp) {
   const char* op = "fused_moe_affine_q4";
   if (!x.is_cuda() || x.scalar_type() != torch::kFloat16)
     throw std::runtime_error("fused_moe_affine_q4: x must be a CUDA float16 tensor");
@@ -551,6 +552,24 @@ torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, 
   if (route_weights.numel() != ntok * top_k || !route_weights.is_cuda() || route_weights.device() != dev)
     throw std::runtime_error("fused_moe_affine_q4: route_weights must be a CUDA tensor with one weight per id");
   if (expert_total < 0) expert_total = expert_first + experts;
+  // shared expert: [gate w, s, b, up w, s, b, down w, s, b] with one expert each
+  const bool has_shared = shared.has_value();
+  const void* sh[9] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  torch::Tensor sw;
+  if (has_shared) {
+    const auto& v = *shared;
+    if (v.size() != 9)
+      throw std::runtime_error("fused_moe_affine_q4: shared must hold 9 tensors (gate, up, down: words, scales, biases)");
+    check_stack({v[0], v[1], v[2]}, "shared gate", inter, hidden, group_size, 1, dev);
+    check_stack({v[3], v[4], v[5]}, "shared up", inter, hidden, group_size, 1, dev);
+    check_stack({v[6], v[7], v[8]}, "shared down", hidden, inter, group_size, 1, dev);
+    for (int i = 0; i < 9; ++i) sh[i] = v[i].data_ptr();
+    if (!shared_weights.has_value() || shared_weights->numel() != ntok || !shared_weights->is_cuda() ||
+        shared_weights->device() != dev)
+      throw std::runtime_error("fused_moe_affine_q4: shared needs shared_weights, one weight per token");
+    sw = shared_weights->to(torch::kFloat16).contiguous();
+  }
+  const int64_t slots = top_k + (has_shared ? 1 : 0);
   c10::cuda::CUDAGuard guard(dev);
   void* stream = c10::cuda::getCurrentCUDAStream(dev.index()).stream();
   torch::Tensor ids = expert_ids.to(torch::kInt32).contiguous();
@@ -573,28 +592,71 @@ torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, 
   if (h.has_value()) {
     hb = *h;
     if (!hb.is_cuda() || hb.device() != dev || hb.scalar_type() != torch::kFloat16 || !hb.is_contiguous() ||
-        hb.numel() < ntok * top_k * inter)
+        hb.numel() < ntok * slots * inter)
       throw std::runtime_error("fused_moe_affine_q4: h must be a contiguous float16 CUDA tensor of at least " +
-                               std::to_string(ntok * top_k * inter) + " elements");
+                               std::to_string(ntok * slots * inter) + " elements");
   } else {
-    hb = torch::empty({ntok, top_k, inter}, x.options());
+    hb = torch::empty({ntok, slots, inter}, x.options());
   }
   int st = gdsq_moe_affine_q4_gate_up(
       gw.data_ptr(), std::get<1>(gate).data_ptr(), std::get<2>(gate).data_ptr(), std::get<0>(up).data_ptr(),
-      std::get<1>(up).data_ptr(), std::get<2>(up).data_ptr(), xc.data_ptr(), ids.data_ptr<int32_t>(),
+      std::get<1>(up).data_ptr(), std::get<2>(up).data_ptr(), sh[0], sh[1], sh[2], sh[3], sh[4], sh[5],
+      xc.data_ptr(), ids.data_ptr<int32_t>(),
       hb.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k), static_cast<int>(inter),
       static_cast<int>(hidden), group_size, static_cast<int>(expert_first), static_cast<int>(experts),
       static_cast<int>(expert_total), stream);
   raise_status(st, op);
-  const int flags = (out_fp32 ? GDSQ_MOE_OUT_F32 : 0) | (accumulate ? GDSQ_MOE_ACCUMULATE : 0);
+  const int flags = (out_fp32 ? GDSQ_MOE_OUT_F32 : 0) | (accumulate ? GDSQ_MOE_ACCUMULATE : 0) |
+                    (clamp ? GDSQ_MOE_CLAMP : 0);
   st = gdsq_moe_affine_q4_down(std::get<0>(down).data_ptr(), std::get<1>(down).data_ptr(),
-                               std::get<2>(down).data_ptr(), hb.data_ptr(), ids.data_ptr<int32_t>(),
-                               rw.data_ptr(), y.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k),
+                               std::get<2>(down).data_ptr(), sh[6], sh[7], sh[8], hb.data_ptr(),
+                               ids.data_ptr<int32_t>(), rw.data_ptr(), has_shared ? sw.data_ptr() : nullptr,
+                               y.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k),
                                static_cast<int>(hidden), static_cast<int>(inter), group_size,
                                static_cast<int>(expert_first), static_cast<int>(experts),
                                static_cast<int>(expert_total), flags, stream);
   raise_status(st, op);
   return y;
+}
+
+// Additive op: the routing tail of moe_route (qwen_moe.py:407-413) on router
+// logits [..., E] fp16 in one launch, plus sigmoid(x . shared_gate).
+// Returns (ids int32 [..., k], weights fp16 [..., k], shared weight fp16 [...] or None).
+py::tuple py_moe_route(torch::Tensor logits, int top_k, c10::optional<torch::Tensor> x,
+                       c10::optional<torch::Tensor> shared_gate) {
+  if (!logits.is_cuda() || logits.scalar_type() != torch::kFloat16 || logits.dim() < 1)
+    throw std::runtime_error("moe_route: logits must be a CUDA float16 tensor [..., num_experts]");
+  const torch::Device dev = logits.device();
+  const int64_t e = logits.size(-1);
+  const int64_t ntok = e > 0 ? logits.numel() / e : 0;
+  c10::cuda::CUDAGuard guard(dev);
+  torch::Tensor lc = logits.contiguous();
+  auto lead = logits.sizes().vec();
+  lead.pop_back();
+  auto ids_shape = lead;
+  ids_shape.push_back(top_k);
+  torch::Tensor ids = torch::empty(ids_shape, logits.options().dtype(torch::kInt32));
+  torch::Tensor w = torch::empty(ids_shape, logits.options());
+  torch::Tensor xc, gc, sw;
+  int hidden = 0;
+  if (shared_gate.has_value()) {
+    if (!x.has_value()) throw std::runtime_error("moe_route: shared_gate needs x");
+    xc = x->contiguous();
+    gc = shared_gate->contiguous();
+    hidden = static_cast<int>(gc.numel());
+    if (!xc.is_cuda() || xc.device() != dev || xc.scalar_type() != torch::kFloat16 || xc.numel() != ntok * hidden ||
+        !gc.is_cuda() || gc.device() != dev || gc.scalar_type() != torch::kFloat16)
+      throw std::runtime_error("moe_route: x [tokens, hidden] and shared_gate [hidden] must be CUDA float16");
+    sw = torch::empty(lead, logits.options());
+  }
+  void* stream = c10::cuda::getCurrentCUDAStream(dev.index()).stream();
+  raise_status(gdsq_moe_route(lc.data_ptr(), static_cast<int>(ntok), static_cast<int>(e), top_k,
+                              shared_gate.has_value() ? xc.data_ptr() : nullptr,
+                              shared_gate.has_value() ? gc.data_ptr() : nullptr, hidden, ids.data_ptr<int32_t>(),
+                              w.data_ptr(), shared_gate.has_value() ? sw.data_ptr() : nullptr, stream),
+               "moe_route");
+  if (shared_gate.has_value()) return py::make_tuple(ids, w, sw);
+  return py::make_tuple(ids, w, py::none());
 }
 
 int py_device_error(int device, bool clear) {
@@ -653,7 +715,11 @@ PYBIND11_MODULE(gds_io_ext, m) {
         py::arg("x"), py::arg("expert_ids"), py::arg("route_weights"), py::arg("gate"), py::arg("up"),
         py::arg("down"), py::arg("group_size") = 128, py::arg("expert_first") = 0, py::arg("expert_total") = -1,
         py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("out_fp32") = false,
-        py::arg("h") = py::none());
+        py::arg("h") = py::none(), py::arg("shared") = py::none(), py::arg("shared_weights") = py::none(),
+        py::arg("clamp") = false);
+  m.def("moe_route", &py_moe_route,
+        "Top-k expert ids, softmax weights and the shared expert's sigmoid gate from router logits (one launch).",
+        py::arg("logits"), py::arg("top_k"), py::arg("x") = py::none(), py::arg("shared_gate") = py::none());
   m.def("handle_from_tensor", &GdsBufferHandle::wrap,
         "Wrap a contiguous CUDA tensor as a GdsBufferHandle (the tensor stays alive with the handle).",
         py::arg("tensor"));

@@ -798,11 +798,11 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
 }
 
 template <int STAGE, int GS>
-int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const DeviceInfo& dev,
-                    cudaStream_t stream) {
+int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const void* sw0, const void* sw1,
+                    const DeviceInfo& dev, cudaStream_t stream) {
   const int cpe = p.K / kChunkCols;
-  const int C = STAGE == 0 ? cpe : p.T * cpe;
-  p.num_items = STAGE == 0 ? p.ntok * p.T * (p.rows / 16) : p.ntok * (p.rows / 32);
+  const int C = STAGE == 0 ? cpe : p.Ts * cpe;
+  p.num_items = STAGE == 0 ? p.ntok * p.Ts * (p.rows / 16) : p.ntok * (p.rows / 32);
   const uint64_t key = ((uint64_t)1 << 63) | ((uint64_t)STAGE << 61) | ((uint64_t)GS << 50) |
                        ((uint64_t)(unsigned)p.num_items << 16) | (uint64_t)(unsigned)C;
   MoePlan plan;
@@ -822,15 +822,24 @@ int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const DeviceInf
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     plans[dev.ordinal][key] = plan;
   }
-  CUtensorMap m0, m1;
+  CUtensorMap m0, m1, s0, s1;
   const int box_rows = STAGE == 0 ? 16 : 32;
   int st = expert_map(dev, w0, p.e_count, p.rows, p.K, box_rows, &m0);
   if (st != GDSQ_OK) return st;
+  m1 = m0;
   if (STAGE == 0) {
     st = expert_map(dev, w1, p.e_count, p.rows, p.K, box_rows, &m1);
     if (st != GDSQ_OK) return st;
-  } else {
-    m1 = m0;
+  }
+  s0 = m0;
+  s1 = m1;
+  if (p.has_shared) {
+    st = expert_map(dev, sw0, 1, p.rows, p.K, box_rows, &s0);
+    if (st != GDSQ_OK) return st;
+    if (STAGE == 0) {
+      st = expert_map(dev, sw1, 1, p.rows, p.K, box_rows, &s1);
+      if (st != GDSQ_OK) return st;
+    }
   }
   auto kernel = moe_affine_kernel<STAGE, GS>;
   cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
@@ -858,7 +867,7 @@ int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const DeviceInf
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kernel, p, m0, m1);
+  e = cudaLaunchKernelEx(&cfg, kernel, p, m0, m1, s0, s1);
   if (e != cudaSuccess) return cuda_fail(e, STAGE == 0 ? "moe gate/up launch" : "moe down launch");
   return GDSQ_OK;
 }
@@ -866,14 +875,26 @@ int launch_moe_fast(MoeParams p, const void* w0, const void* w1, const DeviceInf
 // Shared argument checks and path choice of both MoE stages.  Matrix 0 is
 // gate (stage 0) or down (stage 1); matrix 1 is up (stage 0 only).
 int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, const void* w1,
-                 const void* s1, const void* b1, const void* x, const int32_t* ids,
-                 const void* route, void* out, int ntok, int top_k, int rows, int cols, int group,
-                 int e_first, int e_count, int e_total, int flags, void* stream_v) {
+                 const void* s1, const void* b1, const void* shw0, const void* shs0, const void* shb0,
+                 const void* shw1, const void* shs1, const void* shb1, const void* shared_route,
+                 const void* x, const int32_t* ids, const void* route, void* out, int ntok, int top_k,
+                 int rows, int cols, int group, int e_first, int e_count, int e_total, int flags,
+                 void* stream_v) {
   t_last_error.clear();
   const char* name = stage == 0 ? "moe gate/up" : "moe down";
-  if (ntok < 0 || top_k < 1 || top_k > kMoeMaxSlots)
+  // The shared expert is present when all of its pointers are given.
+  const void* sh_ptrs[7] = {shw0, shs0, shb0, shw1, shs1, shb1, shared_route};
+  const int n_sh = stage == 0 ? 6 : 3;
+  int given = 0;
+  for (int i = 0; i < n_sh; ++i) given += sh_ptrs[i] != nullptr;
+  if (stage == 1) given += shared_route != nullptr;
+  const int n_need = stage == 0 ? 6 : 4;
+  if (given != 0 && given != n_need)
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: shared expert pointers must be all given or all null", name);
+  const int has_shared = given == n_need ? 1 : 0;
+  if (ntok < 0 || top_k < 1 || top_k + has_shared > kMoeMaxSlots)
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: num_tokens %d must be >= 0 and top_k %d in 1..%d", name, ntok,
-                top_k, kMoeMaxSlots);
+                top_k, kMoeMaxSlots - has_shared);
   if (rows <= 0 || cols <= 0)
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: expert matrix shape [%d, %d] must be positive", name, rows, cols);
   if (group <= 0 || group % 8 != 0 || cols % group != 0)
@@ -882,16 +903,20 @@ int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, cons
   if (e_first < 0 || e_count < 1 || e_total < 1 || (long long)e_first + e_count > e_total)
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: resident experts [%d, %d) outside 0..%d", name, e_first,
                 e_first + e_count, e_total);
-  if (flags & ~(kMoeOutF32 | kMoeAccumulate))
+  if (flags & ~(kMoeOutF32 | kMoeAccumulate | kMoeClamp))
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: unknown flags 0x%x", name, flags);
-  const long long pairs = (long long)ntok * top_k;
+  const long long pairs = (long long)ntok * (top_k + has_shared);
   if (pairs * rows > (1ll << 30))
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: %lld outputs is too many for one call", name, pairs * rows);
   if (ntok == 0) return GDSQ_OK;
   if (!w0 || !s0 || !b0 || !x || !ids || !out || (stage == 0 && (!w1 || !s1 || !b1)) || (stage == 1 && !route))
     return fail(GDSQ_ERR_INVALID_VALUE, "%s: null pointer", name);
-  if (!aligned(w0, 4) || (stage == 0 && !aligned(w1, 4)))
+  if (!aligned(w0, 4) || (stage == 0 && !aligned(w1, 4)) ||
+      (has_shared && (!aligned(shw0, 4) || (stage == 0 && !aligned(shw1, 4)))))
     return fail(GDSQ_ERR_MISALIGNED, "%s: expert weights must be 4-byte aligned", name);
+  if (has_shared && (!aligned(shs0, 2) || !aligned(shb0, 2) || (stage == 0 && (!aligned(shs1, 2) || !aligned(shb1, 2))) ||
+                     (stage == 1 && !aligned(shared_route, 2))))
+    return fail(GDSQ_ERR_MISALIGNED, "%s: shared expert scales, biases and weights need 2-byte alignment", name);
   if (!aligned(s0, 2) || !aligned(b0, 2) || (stage == 0 && (!aligned(s1, 2) || !aligned(b1, 2))) ||
       !aligned(x, 2) || (stage == 1 && !aligned(route, 2)))
     return fail(GDSQ_ERR_MISALIGNED, "%s: scales, biases, activations and weights of the route need 2-byte alignment",
@@ -925,26 +950,36 @@ int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, cons
   p.w0 = static_cast<const uint32_t*>(w0);
   p.w1 = static_cast<const uint32_t*>(w1);
   p.group = group;
+  p.has_shared = has_shared;
+  p.Ts = top_k + has_shared;
+  p.ss0 = static_cast<const __half*>(shs0);
+  p.sb0 = static_cast<const __half*>(shb0);
+  p.ss1 = static_cast<const __half*>(shs1);
+  p.sb1 = static_cast<const __half*>(shb1);
+  p.shared_route = static_cast<const __half*>(shared_route);
+  p.sw0 = static_cast<const uint32_t*>(shw0);
+  p.sw1 = static_cast<const uint32_t*>(shw1);
 
   const bool fast = cols % kChunkCols == 0 && rows % (stage == 0 ? 16 : 32) == 0 && aligned(w0, 16) &&
                     (stage == 1 || aligned(w1, 16)) && aligned(x, 16) &&
+                    (!has_shared || (aligned(shw0, 16) && (stage == 1 || aligned(shw1, 16)))) &&
                     (group == 32 || group == 64 || group == 128 || group == 256) &&
-                    moe_smem_layout(stage == 0 ? cols / kChunkCols : top_k * cols / kChunkCols, group,
+                    moe_smem_layout(stage == 0 ? cols / kChunkCols : p.Ts * cols / kChunkCols, group,
                                     kMaxCluster, 2).total <= dev->smem_optin;
   if (fast) {
     if (stage == 0) {
       switch (group) {
-        case 32: return launch_moe_fast<0, 32>(p, w0, w1, *dev, stream);
-        case 64: return launch_moe_fast<0, 64>(p, w0, w1, *dev, stream);
-        case 128: return launch_moe_fast<0, 128>(p, w0, w1, *dev, stream);
-        default: return launch_moe_fast<0, 256>(p, w0, w1, *dev, stream);
+        case 32: return launch_moe_fast<0, 32>(p, w0, w1, shw0, shw1, *dev, stream);
+        case 64: return launch_moe_fast<0, 64>(p, w0, w1, shw0, shw1, *dev, stream);
+        case 128: return launch_moe_fast<0, 128>(p, w0, w1, shw0, shw1, *dev, stream);
+        default: return launch_moe_fast<0, 256>(p, w0, w1, shw0, shw1, *dev, stream);
       }
     }
     switch (group) {
-      case 32: return launch_moe_fast<1, 32>(p, w0, w1, *dev, stream);
-      case 64: return launch_moe_fast<1, 64>(p, w0, w1, *dev, stream);
-      case 128: return launch_moe_fast<1, 128>(p, w0, w1, *dev, stream);
-      default: return launch_moe_fast<1, 256>(p, w0, w1, *dev, stream);
+      case 32: return launch_moe_fast<1, 32>(p, w0, w1, shw0, shw1, *dev, stream);
+      case 64: return launch_moe_fast<1, 64>(p, w0, w1, shw0, shw1, *dev, stream);
+      case 128: return launch_moe_fast<1, 128>(p, w0, w1, shw0, shw1, *dev, stream);
+      default: return launch_moe_fast<1, 256>(p, w0, w1, shw0, shw1, *dev, stream);
     }
   }
   const long long warps = stage == 0 ? pairs * rows : (long long)ntok * rows;
@@ -1102,21 +1137,58 @@ int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void
 
 int gdsq_moe_affine_q4_gate_up(const void* gate_weight, const void* gate_scales, const void* gate_biases,
                                const void* up_weight, const void* up_scales, const void* up_biases,
-                               const void* x, const int32_t* expert_ids, void* h, int num_tokens, int top_k,
-                               int inter_dim, int hidden_dim, int group_size, int expert_first,
-                               int expert_count, int expert_total, void* stream) {
-  return moe_dispatch(0, gate_weight, gate_scales, gate_biases, up_weight, up_scales, up_biases, x,
-                      expert_ids, nullptr, h, num_tokens, top_k, inter_dim, hidden_dim, group_size,
-                      expert_first, expert_count, expert_total, 0, stream);
+                               const void* shared_gate_weight, const void* shared_gate_scales,
+                               const void* shared_gate_biases, const void* shared_up_weight,
+                               const void* shared_up_scales, const void* shared_up_biases, const void* x,
+                               const int32_t* expert_ids, void* h, int num_tokens, int top_k, int inter_dim,
+                               int hidden_dim, int group_size, int expert_first, int expert_count,
+                               int expert_total, void* stream) {
+  return moe_dispatch(0, gate_weight, gate_scales, gate_biases, up_weight, up_scales, up_biases,
+                      shared_gate_weight, shared_gate_scales, shared_gate_biases, shared_up_weight,
+                      shared_up_scales, shared_up_biases, nullptr, x, expert_ids, nullptr, h, num_tokens, top_k,
+                      inter_dim, hidden_dim, group_size, expert_first, expert_count, expert_total, 0, stream);
 }
 
 int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales, const void* down_biases,
-                            const void* h, const int32_t* expert_ids, const void* route_weights, void* y,
-                            int num_tokens, int top_k, int hidden_dim, int inter_dim, int group_size,
-                            int expert_first, int expert_count, int expert_total, int flags, void* stream) {
-  return moe_dispatch(1, down_weight, down_scales, down_biases, nullptr, nullptr, nullptr, h, expert_ids,
-                      route_weights, y, num_tokens, top_k, hidden_dim, inter_dim, group_size, expert_first,
-                      expert_count, expert_total, flags, stream);
+                            const void* shared_down_weight, const void* shared_down_scales,
+                            const void* shared_down_biases, const void* h, const int32_t* expert_ids,
+                            const void* route_weights, const void* shared_weights, void* y, int num_tokens,
+                            int top_k, int hidden_dim, int inter_dim, int group_size, int expert_first,
+                            int expert_count, int expert_total, int flags, void* stream) {
+  return moe_dispatch(1, down_weight, down_scales, down_biases, nullptr, nullptr, nullptr, shared_down_weight,
+                      shared_down_scales, shared_down_biases, nullptr, nullptr, nullptr, shared_weights, h,
+                      expert_ids, route_weights, y, num_tokens, top_k, hidden_dim, inter_dim, group_size,
+                      expert_first, expert_count, expert_total, flags, stream);
+}
+
+int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,
+                   const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
+                   void* shared_weights, void* stream_v) {
+  t_last_error.clear();
+  if (num_tokens < 0 || num_experts < 1 || num_experts > kRouteMaxExperts || top_k < 1 || top_k > 64 ||
+      top_k > num_experts)
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe route: need 0 <= tokens, 1 <= top_k (%d) <= min(64, experts %d), "
+                "experts <= %d", top_k, num_experts, kRouteMaxExperts);
+  if (num_tokens == 0) return GDSQ_OK;
+  if (!logits || !expert_ids || !route_weights) return fail(GDSQ_ERR_INVALID_VALUE, "moe route: null pointer");
+  const bool shared = shared_gate != nullptr;
+  if (shared && (!x || !shared_weights || hidden_dim <= 0 || hidden_dim % 8 != 0))
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe route: the shared gate needs x, an output and hidden_dim %% 8 == 0");
+  if (!aligned(logits, 2) || !aligned(expert_ids, 4) || !aligned(route_weights, 2) ||
+      (shared && (!aligned(x, 16) || !aligned(shared_gate, 16) || !aligned(shared_weights, 2))))
+    return fail(GDSQ_ERR_MISALIGNED, "moe route: logits/weights 2-byte, ids 4-byte, x and the shared gate "
+                "16-byte alignment");
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  const size_t smem = (size_t)(num_experts + 64) * sizeof(float);
+  cudaError_t e = ensure_smem(moe_route_kernel, (int)smem, dev->ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(moe route)");
+  e = launch(moe_route_kernel, dim3(num_tokens), dim3(64), smem, static_cast<cudaStream_t>(stream_v),
+             g_pdl_enabled != 0, static_cast<const __half*>(logits), num_experts, top_k,
+             static_cast<const __half*>(x), static_cast<const __half*>(shared_gate), hidden_dim, expert_ids,
+             static_cast<__half*>(route_weights), static_cast<__half*>(shared_weights));
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "moe route launch");
 }
 
 }  // extern "C"

@@ -19,7 +19,10 @@
 // scales and biases (the layer-file layout, convert_qwen_moe.py:205-253).
 // Only experts [e_first, e_first + e_count) are resident (expert parallelism:
 // each rank holds a contiguous range); slots whose expert lives elsewhere are
-// skipped, so stage 1 yields this rank's partial sum.
+// skipped, so stage 1 yields this rank's partial sum.  Optionally the shared
+// expert (qwen_moe.py:497-510; separate [1][rows][K/8] tensors) rides along
+// as one more slot per token, weighted by sigmoid(x . g) supplied per token,
+// so one pair of launches computes the whole MoE MLP.
 //
 // Schedule (same machinery as the dense fast GEMV in gemv.cuh):
 //   * Work item = 32 output lanes.  Stage 0: rows [r0, r0+16) of gate (lanes
@@ -42,7 +45,8 @@ namespace gdsq {
 constexpr int kMoeMaxSlots = 64;           // top-k limit of one token
 constexpr int kMoeChunkBytes = 128;        // one 256-column chunk of one row
 constexpr int kMoeStageBytes = 32 * kMoeChunkBytes;
-enum : int { kMoeOutF32 = 1, kMoeAccumulate = 2 };
+enum : int { kMoeOutF32 = 1, kMoeAccumulate = 2, kMoeClamp = 4 };
+constexpr int kMoeShared = -2;             // slot code of the shared expert
 
 struct MoeParams {
   const __half* s0;     // scales of matrix 0 (gate in stage 0, down in stage 1)
@@ -63,11 +67,21 @@ struct MoeParams {
   int cs;
   int stages;
   int num_items;
-  int flags;            // stage 1: kMoeOutF32 | kMoeAccumulate
+  int flags;            // stage 1: kMoeOutF32 | kMoeAccumulate | kMoeClamp
+  // Shared expert (has_shared != 0): slot T of every token.
+  int has_shared;
+  int Ts;               // slots per token in h and in stage 1's K: T + has_shared
+  const __half* ss0;    // its scales / biases of matrix 0 [1][rows][K/GS]
+  const __half* sb0;
+  const __half* ss1;    // matrix 1 (stage 0)
+  const __half* sb1;
+  const __half* shared_route;  // [ntok] fp16 weight of the shared slot (stage 1)
   // Generic kernels only: packed words of the matrices (the fast kernels
   // read them through tensor maps).
   const uint32_t* w0;
   const uint32_t* w1;
+  const uint32_t* sw0;
+  const uint32_t* sw1;
   int group;
 };
 
@@ -124,17 +138,28 @@ __device__ __forceinline__ int moe_local_expert(const MoeParams& p, int q) {
   return (z >= 0 && z < p.e_count) ? z : -1;
 }
 
+// Local expert of slot t of token tok: >= 0 routed, kMoeShared, or -1.
+__device__ __forceinline__ int moe_slot_expert(const MoeParams& p, int tok, int t) {
+  if (t >= p.T) return kMoeShared;
+  return moe_local_expert(p, tok * p.T + t);
+}
+
+__device__ __forceinline__ float moe_finish(float v, int flags) {
+  return (flags & kMoeClamp) ? fminf(fmaxf(v, -65504.0f), 65504.0f) : v;
+}
+
 template <int STAGE, int GS>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     moe_affine_kernel(const MoeParams p, const __grid_constant__ CUtensorMap map0,
-                      const __grid_constant__ CUtensorMap map1) {
+                      const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap smap0,
+                      const __grid_constant__ CUtensorMap smap1) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int cs = p.cs;
   const int S = p.stages;
   const int cpe = p.K / kChunkCols;               // chunks per expert row
-  const int C = STAGE == 0 ? cpe : p.T * cpe;     // chunks per item
-  const int Kx = STAGE == 0 ? p.K : p.T * p.K;    // activation columns per token
+  const int C = STAGE == 0 ? cpe : p.Ts * cpe;    // chunks per item
+  const int Kx = STAGE == 0 ? p.K : p.Ts * p.K;   // activation columns per token
   const MoeSmemLayout L = moe_smem_layout(C, GS, cs, S);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -169,6 +194,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     if (warp == 0) {
       prefetch_tensor_map(&map0);
       if (STAGE == 0) prefetch_tensor_map(&map1);
+      if (p.has_shared) {
+        prefetch_tensor_map(&smap0);
+        if (STAGE == 0) prefetch_tensor_map(&smap1);
+      }
     }
   }
   __syncwarp();
@@ -189,9 +218,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
         continue;
       }
       const int it = cluster + p_ii * nclusters;
-      const int z = STAGE == 0 ? moe_local_expert(p, it / rgs)
-                               : moe_local_expert(p, (it / rgs) * p.T + (c0 + wc0 + p_j) / cpe);
-      if (z >= 0) return z;
+      const int z = STAGE == 0 ? moe_slot_expert(p, (it / rgs) / p.Ts, (it / rgs) % p.Ts)
+                               : moe_slot_expert(p, it / rgs, (c0 + wc0 + p_j) / cpe);
+      if (z != -1) return z;
       if (STAGE == 0) {
         p_j = 0;
         ++p_ii;
@@ -202,8 +231,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     return -1;
   };
   auto issue_next = [&]() -> bool {
-    const int z = seek();
-    if (z < 0) return false;
+    const int zs = seek();
+    if (zs == -1) return false;
+    const bool shared = zs == kMoeShared;
+    const int z = shared ? 0 : zs;
     const int it = cluster + p_ii * nclusters;
     const int chunk = c0 + wc0 + p_j;
     if (lane == 0) {
@@ -211,12 +242,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       mbar_arrive_expect_tx(&bars[p_stage], kMoeStageBytes);
       if constexpr (STAGE == 0) {
         const int row0 = (it % rgs) * 16;
-        tma_load_3d(dst, &map0, chunk * (kMoeChunkBytes / 8), row0, z, &bars[p_stage], policy);
-        tma_load_3d(dst + 16 * kMoeChunkBytes, &map1, chunk * (kMoeChunkBytes / 8), row0, z,
+        tma_load_3d(dst, shared ? &smap0 : &map0, chunk * (kMoeChunkBytes / 8), row0, z, &bars[p_stage], policy);
+        tma_load_3d(dst + 16 * kMoeChunkBytes, shared ? &smap1 : &map1, chunk * (kMoeChunkBytes / 8), row0, z,
                     &bars[p_stage], policy);
       } else {
         const int row0 = (it % rgs) * 32;
-        tma_load_3d(dst, &map0, (chunk % cpe) * (kMoeChunkBytes / 8), row0, z, &bars[p_stage], policy);
+        tma_load_3d(dst, shared ? &smap0 : &map0, (chunk % cpe) * (kMoeChunkBytes / 8), row0, z, &bars[p_stage],
+                    policy);
       }
     }
     ++p_j;
@@ -253,10 +285,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     int tok, row0, pair = 0, zi = 0;
     if constexpr (STAGE == 0) {
       pair = it / rgs;
-      tok = pair / p.T;
+      tok = pair / p.Ts;
       row0 = (it % rgs) * 16;
-      zi = moe_local_expert(p, pair);
-      if (zi < 0) continue;  // uniform over the cluster
+      zi = moe_slot_expert(p, tok, pair % p.Ts);
+      if (zi == -1) continue;  // uniform over the cluster
     } else {
       tok = it / rgs;
       row0 = (it % rgs) * 32;
@@ -266,10 +298,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       stage_x_affine<GS>(p.x + (size_t)tok * Kx, xs, xsum, 1, 1, Kx, c0 * kChunkCols,
                          cslice * kChunkCols, ld);
       if constexpr (STAGE == 1) {
-        for (int t = threadIdx.x; t < p.T; t += blockDim.x) {
-          const int q = tok * p.T + t;
-          slot_z[t] = moe_local_expert(p, q);
-          slot_w[t] = __half2float(p.route[q]);
+        for (int t = threadIdx.x; t < p.Ts; t += blockDim.x) {
+          slot_z[t] = moe_slot_expert(p, tok, t);
+          slot_w[t] = __half2float(t < p.T ? p.route[tok * p.T + t] : p.shared_route[tok]);
         }
       }
       staged_tok = tok;
@@ -280,17 +311,21 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       const int g = idx - r * gsl;
       uint32_t v = 0;
       if constexpr (STAGE == 0) {
-        const __half* sc = r < 16 ? p.s0 : p.s1;
-        const __half* bi = r < 16 ? p.b0 : p.b1;
-        const size_t gi = ((size_t)zi * p.rows + row0 + (r & 15)) * G + gbase + g;
+        const bool sh = zi == kMoeShared;
+        const __half* sc = r < 16 ? (sh ? p.ss0 : p.s0) : (sh ? p.ss1 : p.s1);
+        const __half* bi = r < 16 ? (sh ? p.sb0 : p.b0) : (sh ? p.sb1 : p.b1);
+        const size_t gi = ((size_t)(sh ? 0 : zi) * p.rows + row0 + (r & 15)) * G + gbase + g;
         v = (uint32_t)__half_as_ushort(sc[gi]) | ((uint32_t)__half_as_ushort(bi[gi]) << 16);
       } else {
         const int gg = gbase + g;          // group index over the token's T*K columns
         const int t = gg / G;
         const int z = slot_z[t];
-        if (z >= 0) {
-          const size_t gi = ((size_t)z * p.rows + row0 + r) * G + (gg - t * G);
-          v = (uint32_t)__half_as_ushort(p.s0[gi]) | ((uint32_t)__half_as_ushort(p.b0[gi]) << 16);
+        if (z != -1) {
+          const bool sh = z == kMoeShared;
+          const size_t gi = ((size_t)(sh ? 0 : z) * p.rows + row0 + r) * G + (gg - t * G);
+          const __half* sc = sh ? p.ss0 : p.s0;
+          const __half* bi = sh ? p.sb0 : p.b0;
+          v = (uint32_t)__half_as_ushort(sc[gi]) | ((uint32_t)__half_as_ushort(bi[gi]) << 16);
         }
       }
       sb[r * L.sb_stride + g] = v;
@@ -303,7 +338,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       float wt = 1.f;
       if constexpr (STAGE == 1) {
         const int t = (c0 + cl) / cpe;
-        if (slot_z[t] < 0) continue;
+        if (slot_z[t] == -1) continue;
         wt = slot_w[t];
       }
       if (ok && !mbar_wait(&bars[stage], phase)) {
@@ -371,10 +406,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
           const float v = fin[threadIdx.x];
           if (p.flags & kMoeOutF32) {
             float* y = static_cast<float*>(p.out);
-            y[o] = (p.flags & kMoeAccumulate) ? y[o] + v : v;
+            y[o] = moe_finish((p.flags & kMoeAccumulate) ? y[o] + v : v, p.flags);
           } else {
             __half* y = static_cast<__half*>(p.out);
-            y[o] = __float2half_rn((p.flags & kMoeAccumulate) ? __half2float(y[o]) + v : v);
+            y[o] = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + v : v, p.flags));
           }
         }
       }
@@ -423,16 +458,19 @@ __global__ void __launch_bounds__(256) moe_gate_up_generic_kernel(const MoeParam
   const long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   pdl_launch_dependents();
   pdl_wait_primary();
-  if (gw >= (long long)p.ntok * p.T * p.rows) return;
+  if (gw >= (long long)p.ntok * p.Ts * p.rows) return;
   const int pair = static_cast<int>(gw / p.rows);
   const int row = static_cast<int>(gw - (long long)pair * p.rows);
-  const int z = moe_local_expert(p, pair);
-  if (z < 0) return;
+  const int z = moe_slot_expert(p, pair / p.Ts, pair % p.Ts);
+  if (z == -1) return;
+  const bool sh = z == kMoeShared;
   const int G = p.K / p.group;
-  const size_t r = (size_t)z * p.rows + row;
-  const __half* x = p.x + (size_t)(pair / p.T) * p.K;
-  const float g = moe_row_dot(p.w0 + r * (p.K / 8), p.s0 + r * G, p.b0 + r * G, x, p.K, p.group, lane);
-  const float u = moe_row_dot(p.w1 + r * (p.K / 8), p.s1 + r * G, p.b1 + r * G, x, p.K, p.group, lane);
+  const size_t r = (size_t)(sh ? 0 : z) * p.rows + row;
+  const __half* x = p.x + (size_t)(pair / p.Ts) * p.K;
+  const float g = moe_row_dot((sh ? p.sw0 : p.w0) + r * (p.K / 8), (sh ? p.ss0 : p.s0) + r * G,
+                              (sh ? p.sb0 : p.b0) + r * G, x, p.K, p.group, lane);
+  const float u = moe_row_dot((sh ? p.sw1 : p.w1) + r * (p.K / 8), (sh ? p.ss1 : p.s1) + r * G,
+                              (sh ? p.sb1 : p.b1) + r * G, x, p.K, p.group, lane);
   if (lane == 0) {
     const float gh = __half2float(__float2half_rn(g));
     const __half sg = __float2half_rn(gh / (1.0f + expf(-gh)));
@@ -452,23 +490,135 @@ __global__ void __launch_bounds__(256) moe_down_generic_kernel(const MoeParams p
   const int row = static_cast<int>(gw - (long long)tok * p.rows);
   const int G = p.K / p.group;
   float acc = 0.f;
-  for (int t = 0; t < p.T; ++t) {
-    const int q = tok * p.T + t;
-    const int z = moe_local_expert(p, q);
-    if (z < 0) continue;
-    const size_t r = (size_t)z * p.rows + row;
-    const float d = moe_row_dot(p.w0 + r * (p.K / 8), p.s0 + r * G, p.b0 + r * G,
-                                p.x + (size_t)q * p.K, p.K, p.group, lane);
-    acc = fmaf(__half2float(p.route[q]), d, acc);
+  for (int t = 0; t < p.Ts; ++t) {
+    const int z = moe_slot_expert(p, tok, t);
+    if (z == -1) continue;
+    const bool sh = z == kMoeShared;
+    const size_t r = (size_t)(sh ? 0 : z) * p.rows + row;
+    const float d = moe_row_dot((sh ? p.sw0 : p.w0) + r * (p.K / 8), (sh ? p.ss0 : p.s0) + r * G,
+                                (sh ? p.sb0 : p.b0) + r * G, p.x + ((size_t)tok * p.Ts + t) * p.K, p.K, p.group,
+                                lane);
+    const float wt = __half2float(t < p.T ? p.route[tok * p.T + t] : p.shared_route[tok]);
+    acc = fmaf(wt, d, acc);
   }
   if (lane == 0) {
     const size_t o = (size_t)tok * p.rows + row;
     if (p.flags & kMoeOutF32) {
       float* y = static_cast<float*>(p.out);
-      y[o] = (p.flags & kMoeAccumulate) ? y[o] + acc : acc;
+      y[o] = moe_finish((p.flags & kMoeAccumulate) ? y[o] + acc : acc, p.flags);
     } else {
       __half* y = static_cast<__half*>(p.out);
-      y[o] = __float2half_rn((p.flags & kMoeAccumulate) ? __half2float(y[o]) + acc : acc);
+      y[o] = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + acc : acc, p.flags));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Routing tail of moe_route (qwen_moe.py:407-413) on the router logits that
+// F.linear produced: top-k (largest first; equal logits by lower expert
+// index), softmax of the k logits in fp32 cast to fp16; and the shared
+// expert's weight sigmoid(fp16(x . g)) (qwen_moe.py:505-509).  One CTA per
+// token: warp 0 selects, warp 1 computes the shared gate.  Replaces the
+// topk / sort / softmax / cast / linear / sigmoid chain of small torch
+// kernels (and their host-visible ids) with one launch.
+constexpr int kRouteMaxExperts = 4096;
+
+__global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict__ logits, int E, int K,
+                                                       const __half* __restrict__ x,
+                                                       const __half* __restrict__ g, int H, int* ids,
+                                                       __half* weights, __half* shared_w) {
+  extern __shared__ float vals[];  // E logits of this token
+  const int tok = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  if (warp == 0) {
+    for (int i = lane; i < E; i += 32) vals[i] = __half2float(logits[(size_t)tok * E + i]);
+    __syncwarp();
+    // Each lane tracks the best of its own strided elements.
+    auto lane_best = [&](float* bv, int* bi) {
+      *bv = -INFINITY;
+      *bi = 0x7fffffff;
+      for (int i = lane; i < E; i += 32) {
+        const float v = vals[i];
+        if (v > *bv) {  // strided order: the first (lowest index) wins ties
+          *bv = v;
+          *bi = i;
+        }
+      }
+    };
+    float bv;
+    int bi;
+    lane_best(&bv, &bi);
+    float sel_v = 0.f;  // lane r keeps the r-th selected logit
+    int sel_i = 0;
+    for (int r = 0; r < K; ++r) {
+      float v = bv;
+      int i = bi;
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, m);
+        if (ov > v || (ov == v && oi < i)) {
+          v = ov;
+          i = oi;
+        }
+      }
+      if ((r & 31) == lane) {
+        sel_v = v;
+        sel_i = i;
+      }
+      if ((i & 31) == lane) {  // the owner removes the winner and rescans
+        vals[i] = -INFINITY;
+        lane_best(&bv, &bi);
+      }
+      __syncwarp();
+      if (r == 31 && K > 32) {  // lanes now hold selections 0..31: emit them before reuse
+        ids[(size_t)tok * K + lane] = sel_i;
+        vals[E + lane] = sel_v;  // park the value for the softmax
+      }
+    }
+    // softmax over the K selected logits (the first is the largest)
+    __syncwarp();
+    if (K > 32) {
+      if (lane < K - 32) {
+        ids[(size_t)tok * K + 32 + lane] = sel_i;
+        vals[E + 32 + lane] = sel_v;
+      }
+    } else if (lane < K) {
+      ids[(size_t)tok * K + lane] = sel_i;
+      vals[E + lane] = sel_v;
+    }
+    __syncwarp();
+    const float mx = vals[E];
+    float e0 = lane < K ? expf(vals[E + lane] - mx) : 0.f;
+    float e1 = lane + 32 < K ? expf(vals[E + 32 + lane] - mx) : 0.f;
+    float sum = e0 + e1;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    if (lane < K) weights[(size_t)tok * K + lane] = __float2half_rn(e0 / sum);
+    if (lane + 32 < K) weights[(size_t)tok * K + 32 + lane] = __float2half_rn(e1 / sum);
+  } else if (g != nullptr) {
+    float acc = 0.f;
+    const __half* xr = x + (size_t)tok * H;
+    for (int j = lane * 8; j < H; j += 32 * 8) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(xr + j);
+      const uint4 gv = *reinterpret_cast<const uint4*>(g + j);
+      const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+      const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a = __half22float2(u32_as_h2(xs[q]));
+        const float2 b = __half22float2(u32_as_h2(gs[q]));
+        acc = fmaf(a.x, b.x, fmaf(a.y, b.y, acc));
+      }
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) {
+      const float v = __half2float(__float2half_rn(acc));  // F.linear's fp16 output
+      shared_w[tok] = __float2half_rn(1.0f / (1.0f + expf(-v)));
     }
   }
 }

@@ -58,7 +58,8 @@ GDSQ_API const char* gdsq_status_string(int status);
 GDSQ_API const char* gdsq_last_error(void);
 
 /* Reads the device-side error word of `device` (bit 1: a bounded wait on an
- * async copy gave up; bit 2: a kernel rejected its arguments).  Synchronises
+ * async copy gave up; bit 2: a kernel rejected its arguments; bit 4: an index
+ * read from device memory, a MoE expert id, was out of range).  Synchronises
  * the device.  clear != 0 resets the word afterwards. */
 GDSQ_API int gdsq_device_error(int device, int clear, int* out_bits);
 
@@ -121,26 +122,50 @@ GDSQ_API int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, c
 
 /* h[t][k][i] = fp16(silu(fp16(gate_e x_t)[i]) * fp16(up_e x_t)[i]), e = ids[t][k].
  * gate/up rows = inter_dim, cols = hidden_dim; x [num_tokens][hidden_dim] fp16;
- * h [num_tokens][top_k][inter_dim] fp16 (entries of non-resident slots are
- * left unwritten). */
+ * h [num_tokens][S][inter_dim] fp16 with S = top_k, or top_k + 1 when the
+ * shared expert is given (its six shared_* pointers: [1][rows][cols/8] words,
+ * [1][rows][cols/group_size] scales and biases; all six null = none); slot
+ * top_k is then the shared expert (qwen_moe.py:497-503).  Entries of
+ * non-resident slots are left unwritten. */
 GDSQ_API int gdsq_moe_affine_q4_gate_up(const void* gate_weight, const void* gate_scales,
                                         const void* gate_biases, const void* up_weight,
-                                        const void* up_scales, const void* up_biases, const void* x,
-                                        const int32_t* expert_ids, void* h, int num_tokens, int top_k,
-                                        int inter_dim, int hidden_dim, int group_size, int expert_first,
-                                        int expert_count, int expert_total, void* stream);
+                                        const void* up_scales, const void* up_biases,
+                                        const void* shared_gate_weight, const void* shared_gate_scales,
+                                        const void* shared_gate_biases, const void* shared_up_weight,
+                                        const void* shared_up_scales, const void* shared_up_biases,
+                                        const void* x, const int32_t* expert_ids, void* h, int num_tokens,
+                                        int top_k, int inter_dim, int hidden_dim, int group_size,
+                                        int expert_first, int expert_count, int expert_total, void* stream);
 
 #define GDSQ_MOE_OUT_F32 1    /* y is fp32 instead of fp16 */
 #define GDSQ_MOE_ACCUMULATE 2 /* y += result instead of y = result */
+#define GDSQ_MOE_CLAMP 4      /* clamp to +-65504 before storing (qwen_moe.py:514) */
 
-/* y[t][j] = sum over resident slots k of route_weights[t][k] * (down_e h[t][k])[j],
- * summed in fp32.  down rows = hidden_dim, cols = inter_dim; route_weights
- * [num_tokens][top_k] fp16; y [num_tokens][hidden_dim]. */
+/* y[t][j] = sum over resident slots k of route_weights[t][k] * (down_e h[t][k])[j]
+ * (+ shared_weights[t] * (shared_down h[t][top_k])[j] when the shared expert's
+ * three shared_down_* pointers and shared_weights [num_tokens] fp16 are
+ * given), summed in fp32.  down rows = hidden_dim, cols = inter_dim;
+ * route_weights [num_tokens][top_k] fp16; y [num_tokens][hidden_dim].  h must
+ * have been produced with the same shared-expert choice. */
 GDSQ_API int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales,
-                                     const void* down_biases, const void* h, const int32_t* expert_ids,
-                                     const void* route_weights, void* y, int num_tokens, int top_k,
+                                     const void* down_biases, const void* shared_down_weight,
+                                     const void* shared_down_scales, const void* shared_down_biases,
+                                     const void* h, const int32_t* expert_ids, const void* route_weights,
+                                     const void* shared_weights, void* y, int num_tokens, int top_k,
                                      int hidden_dim, int inter_dim, int group_size, int expert_first,
                                      int expert_count, int expert_total, int flags, void* stream);
+
+/* The routing tail of moe_route (qwen_moe.py:407-413) on router logits fp16
+ * [num_tokens][num_experts] (the output of F.linear(x, W_router)): expert_ids
+ * int32 [num_tokens][top_k] of the top_k largest logits, largest first (equal
+ * logits: lower expert index first), route_weights fp16 = softmax of those
+ * logits in fp32.  With shared_gate fp16 [hidden_dim] (and x fp16
+ * [num_tokens][hidden_dim], 16-byte aligned) also shared_weights fp16
+ * [num_tokens] = sigmoid(fp16(x . shared_gate)) (qwen_moe.py:505-509).
+ * num_experts <= 4096, top_k <= 64. */
+GDSQ_API int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,
+                            const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
+                            void* shared_weights, void* stream);
 
 #ifdef __cplusplus
 }

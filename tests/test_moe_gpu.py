@@ -241,3 +241,111 @@ def test_fused_moe_binding_shapes(ext, cuda):
         ext.fused_moe_affine_q4(x, ids.to(cuda), w.to(cuda), dev[0], dev[1], dev[2], accumulate=True)
     with pytest.raises(RuntimeError, match="weight shape"):
         ext.fused_moe_affine_q4(x, ids.to(cuda), w.to(cuda), dev[0], dev[0], dev[0])
+
+
+def test_moe_layer_decode_matches_reference_layer(cuda):
+    """gdsllm_b200.moe.moe_mlp_decode (routing, routed experts, shared expert,
+    clamp) against oracle.moe_mlp_reference on the same routing."""
+    from gdsllm_b200 import moe
+    experts, hidden, inter, group, top_k = 16, 4096, 1024, 128, 10
+    cpu, dev = _stacks(experts, hidden, inter, group, seed=91, device=cuda)
+    scpu, sdev = _stacks(1, hidden, inter, group, seed=95, device=cuda)
+    g = torch.Generator().manual_seed(4)
+    router = (torch.randn(experts, hidden, generator=g) / hidden ** 0.5).half()
+    sgate = (torch.randn(1, hidden, generator=g) / hidden ** 0.5).half()
+    layer = moe.MoeLayer(router=router.to(cuda), gate=dev[0], up=dev[1], down=dev[2], group=group,
+                         shared=sdev, shared_gate=sgate.to(cuda))
+    x = synth.activations(1, hidden, seed=6).view(1, 1, hidden)
+    y = moe.moe_mlp_decode(x.to(cuda), layer, top_k)
+    ids, w, _ = moe.route(x.view(1, hidden).to(cuda), layer.router, top_k, layer.shared_gate)
+    torch.cuda.synchronize()
+    ref = oracle.moe_mlp_reference(x.view(1, hidden).numpy(), ids.cpu().numpy(), w.cpu().numpy(), *cpu, group,
+                                   shared=scpu, shared_gate_w=sgate.numpy())
+    # bar: the routed bar of the decode-sequence test plus the shared expert's
+    # own GEMV bar (one more expert, weight sigmoid <= 1)
+    idn = np.concatenate([ids.cpu().numpy(), np.zeros((1, 1), np.int32)], axis=1)
+    got = y.view(1, hidden).float().cpu().numpy().astype(np.float64)
+    h_ref, _, _ = oracle.moe_gate_up_exact(x.view(1, hidden).numpy(), ids.cpu().numpy(), cpu[0], cpu[1], group)
+    _, bar = oracle.moe_down_exact(h_ref, ids.cpu().numpy(), w.cpu().numpy(), cpu[2], group)
+    hs, _, _ = oracle.moe_gate_up_exact(x.view(1, hidden).numpy(), np.zeros((1, 1), np.int32), scpu[0], scpu[1], group)
+    _, sbar = oracle.moe_down_exact(hs, np.zeros((1, 1), np.int32), np.ones((1, 1), np.float16), scpu[2], group)
+    scale = np.abs(ref.astype(np.float64)).max()
+    tol = 3 * (bar + sbar)[:, None] + (top_k + 3) * _ulp16(ref.astype(np.float64)) + 2e-3 * scale
+    err = np.abs(got - ref.astype(np.float64))
+    assert np.isfinite(got).all()
+    assert (err <= tol).all(), f"worst err/bar {(err / tol).max():.3f}"
+    assert idn.shape == (1, top_k + 1)
+
+
+@pytest.mark.parametrize("ntok,top_k", [(1, 10), (8, 10), (3, 4)])
+def test_moe_shared_expert_slot(gdsq, cuda, ntok, top_k):
+    """The shared expert as slot top_k of the same two launches equals the
+    routed sum plus sigmoid-weighted shared expert (qwen_moe.py:497-510)."""
+    experts, hidden, inter, group = 16, 2048, 512, 128
+    cpu, dev = _stacks(experts, hidden, inter, group, seed=61 + ntok, device=cuda)
+    scpu, sdev = _stacks(1, hidden, inter, group, seed=71, device=cuda)
+    ids, w = _routing(ntok, top_k, experts, seed=ntok)
+    sw = torch.rand(ntok, generator=torch.Generator().manual_seed(2)).half()
+    x = synth.activations(ntok, hidden, seed=9)
+    h = gdsq.moe_gate_up(dev[0], dev[1], x.to(cuda), ids.to(cuda), group, shared=(sdev[0], sdev[1]))
+    y = gdsq.moe_down(dev[2], h, ids.to(cuda), w.to(cuda), group, flags=gdsq.MOE_OUT_F32, shared=sdev[2],
+                      shared_weights=sw.to(cuda))
+    torch.cuda.synchronize()
+    assert h.shape == (ntok, top_k + 1, inter)
+    _check_h(h[:, :top_k], cpu, ids.numpy(), x.numpy(), group)
+    zero = np.zeros((ntok, 1), np.int32)
+    _check_h(h[:, top_k:], scpu, zero, x.numpy(), group)
+    hn = h.cpu().numpy()
+    y_r, bar_r = oracle.moe_down_exact(hn[:, :top_k], ids.numpy(), w.numpy(), cpu[2], group)
+    y_s, bar_s = oracle.moe_down_exact(hn[:, top_k:], zero, sw.numpy().reshape(-1, 1), scpu[2], group)
+    got = y.cpu().numpy().astype(np.float64)
+    err = np.abs(got - (y_r + y_s))
+    tol = (bar_r + bar_s)[:, None] + 1e-6 * np.abs(y_r + y_s).max()
+    assert (err <= tol).all(), f"worst err/bar {(err / tol).max():.3f}"
+
+
+def test_moe_clamp_flag(gdsq, cuda):
+    experts, hidden, inter, group = 2, 1024, 256, 128
+    cpu, dev = _stacks(experts, hidden, inter, group, seed=5, device=cuda)
+    ids = torch.tensor([[0, 1]], dtype=torch.int32)
+    w = torch.tensor([[30000.0, 30000.0]], dtype=torch.float16)   # drives |y| past the fp16 range
+    x = (synth.activations(1, hidden, seed=3) * 8).half()
+    h = gdsq.moe_gate_up(dev[0], dev[1], x.to(cuda), ids.to(cuda), group)
+    y_inf = gdsq.moe_down(dev[2], h, ids.to(cuda), w.to(cuda), group)
+    y_cl = gdsq.moe_down(dev[2], h, ids.to(cuda), w.to(cuda), group, flags=gdsq.MOE_CLAMP)
+    torch.cuda.synchronize()
+    assert torch.isinf(y_inf).any(), "test input does not overflow fp16"
+    assert torch.isfinite(y_cl).all() and y_cl.abs().max().item() == 65504.0
+
+
+@pytest.mark.parametrize("ntok,experts,top_k", [(1, 512, 10), (8, 512, 10), (5, 64, 7), (2, 128, 40)])
+def test_moe_route_kernel_matches_torch_topk(gdsq, cuda, ntok, experts, top_k):
+    """Top-k set exactly as torch.topk on the same fp16 logits (ties at the
+    boundary excepted, there any equal logit is a valid pick), softmax weights
+    and the shared gate within fp16 rounding."""
+    import torch.nn.functional as F
+    hidden = 4096
+    g = torch.Generator(device=cuda).manual_seed(ntok + experts)
+    router = (torch.randn(experts, hidden, generator=g, device=cuda) / hidden ** 0.5).half()
+    sgate = (torch.randn(hidden, generator=g, device=cuda) / hidden ** 0.5).half()
+    x = torch.randn(ntok, hidden, generator=g, device=cuda).half()
+    logits = F.linear(x, router)
+    ids, w, sw = gdsq.moe_route(logits, top_k, x, sgate)
+    tv, ti = torch.topk(logits, top_k, dim=-1)
+    tw = F.softmax(tv.float(), dim=-1).half()
+    tsw = torch.sigmoid(F.linear(x, sgate.view(1, -1))).view(-1)
+    torch.cuda.synchronize()
+    lg = logits.float().cpu()
+    for t in range(ntok):
+        mine, ref = set(ids[t].tolist()), set(ti[t].tolist())
+        chosen = lg[t, ids[t].long().cpu()]
+        rest = torch.ones(experts, dtype=torch.bool)
+        rest[ids[t].long().cpu()] = False
+        assert lg[t][rest].max() <= chosen.min(), "not a top-k set"
+        if mine != ref:  # only an exact tie at the boundary may differ
+            boundary = tv[t, -1].float().item()
+            assert all(abs(lg[t, e].item() - boundary) == 0 for e in mine ^ ref), (t, mine ^ ref)
+        # weights follow the ids' order: compare through the logits they belong to
+        assert torch.equal(lg[t, ids[t].long().cpu()], tv[t].float().cpu()), "order differs from torch.topk"
+    assert (w.float() - tw.float()).abs().max().item() <= 2 * 2 ** -11
+    assert (sw.float() - tsw.float()).abs().max().item() <= 2 * 2 ** -11

@@ -1,0 +1,100 @@
+"""Expert-parallel MoE and tensor-parallel GEMV on 2 GPUs over NCCL, each
+rank's CUDA kernels + one all-reduce, against the single-GPU result computed
+on rank 0.  Skipped unless two GPUs are visible (a box with one GPU cannot
+run two NCCL ranks)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from gdsllm_b200 import capi, ep, moe, synth, tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        res = {}
+        # ---- expert parallel MoE layer ----
+        experts, hidden, inter, group = 32, 2048, 512, 128
+
+        def st(rows, cols, seed, e):
+            return tuple(t.to(dev) for t in synth.affine_q4_weight(rows, cols, group=group, seed=seed, lead=(e,)))
+
+        gate, up, down = st(inter, hidden, 1, experts), st(inter, hidden, 2, experts), st(hidden, inter, 3, experts)
+        shared = (st(inter, hidden, 4, 1), st(inter, hidden, 5, 1), st(hidden, inter, 6, 1))
+        g = torch.Generator().manual_seed(7)
+        router = (torch.randn(experts, hidden, generator=g) / hidden ** 0.5).half().to(dev)
+        sgate = (torch.randn(1, hidden, generator=g) / hidden ** 0.5).half().to(dev)
+        first, count = ep.expert_range(rank, world, experts)
+        local = moe.MoeLayer(router=router, gate=ep.local_stack(gate, rank, world), up=ep.local_stack(up, rank, world),
+                             down=ep.local_stack(down, rank, world), group=group, expert_first=first,
+                             expert_total=experts, shared=shared, shared_gate=sgate)
+        x = synth.activations(8, hidden, seed=8).to(dev)
+        y_ep = ep.ExpertParallelMoE(local, top_k=10)(x)
+        full = moe.MoeLayer(router=router, gate=gate, up=up, down=down, group=group, shared=shared, shared_gate=sgate)
+        y_one = moe.moe_mlp_decode(x, full, 10)
+        res["ep"] = (y_ep.float() - y_one.float()).abs().max().item()
+        res["ep_scale"] = y_one.float().abs().max().item()
+        # ---- tensor parallel Q4_0: column split then row split + all-reduce ----
+        n, k = 4096, 8192
+        w = synth.q4_0_weight(n, k, seed=11).to(dev)
+        xv = synth.activations(1, k, seed=12).to(dev)
+        col = tp.ColumnParallelGemv(tp.split_rows(w, rank, world), n, k, "q4_0", rank, world)
+        y_col = col(xv)
+        parts = [torch.empty_like(y_col) for _ in range(world)]
+        dist.all_gather(parts, y_col)
+        y_full = capi.gemv_q4_0(w, xv, n, k)
+        res["col"] = (torch.cat(parts, dim=1).float() - y_full.float()).abs().max().item()
+        res["col_scale"] = y_full.float().abs().max().item()
+        wt = synth.q4_0_weight(k, n, seed=13).to(dev)  # [8192, 4096]: K = 4096 split
+        xk = synth.activations(1, n, seed=14).to(dev)
+        row = tp.RowParallelGemv(tp.split_k_gguf(wt, n, "q4_0", rank, world), k, n, "q4_0", rank, world)
+        kl = n // world
+        y_row = row(xk[:, rank * kl:(rank + 1) * kl].contiguous())
+        y_ref = capi.gemv_q4_0(wt, xk, k, n)
+        res["row"] = (y_row.float() - y_ref.float()).abs().max().item()
+        res["row_scale"] = y_ref.float().abs().max().item()
+        torch.cuda.synchronize()
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_and_tensor_parallel_on_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, res in out.items():
+        # EP: fp32 partial sums reordered across ranks, one fp16 rounding
+        assert res["ep"] <= 2e-3 * res["ep_scale"] + 1e-3, (rank, res)
+        # column split: the same rows; a shard may take another K split, so
+        # the fp32 summation order (not the math) can differ
+        assert res["col"] <= 2e-3 * res["col_scale"] + 1e-3, (rank, res)
+        # row split: two fp16 partials added (one extra rounding each)
+        assert res["row"] <= 4e-3 * res["row_scale"] + 2e-3, (rank, res)
