@@ -84,10 +84,12 @@ def load_peaks():
 # distributed plumbing
 
 class Dist:
-    def __init__(self):
+    def __init__(self, sample_clocks: bool = True):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        # rank 0 samples its GPU's clocks; started before any GPU work
+        self.clocks = ClockSampler(self.local) if (sample_clocks and self.rank == 0) else None
         torch.cuda.set_device(self.local)
         self.device = torch.device("cuda", self.local)
         if self.world > 1:
@@ -110,6 +112,8 @@ class Dist:
         return float(t.item())
 
     def close(self):
+        if self.clocks is not None:
+            self.clocks.close()
         if self.world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
@@ -119,47 +123,51 @@ class Dist:
 # clocks during the timed region
 
 class ClockSampler:
-    """nvidia-smi samples every 100 ms; only samples whose timestamp falls
-    inside [start(), stop()] count."""
+    """nvidia-smi samples every 100 ms for the whole run (started before any
+    GPU work, so that its start-up -- NVML initialisation of the box -- never
+    overlaps a timed region); window() returns the statistics of the samples
+    whose timestamps fall inside one timed region."""
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
+    def __init__(self, device_index: int):
         self.proc = None
+        self.lines = []
         cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
-        self.target = str(device.index)
+        target = str(device_index)
         if cvd:
             ids = [c.strip() for c in cvd.split(",") if c.strip()]
-            if device.index < len(ids):
-                self.target = ids[device.index]
-
-    def start(self):
+            if device_index < len(ids):
+                target = ids[device_index]
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", self.target],
+                 "-lms", "100", "-i", target],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
-        time.sleep(0.5)
+            return
+        import threading
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
+
+    def start(self):
         self.t0 = time.time()
 
     def stop(self):
         if self.proc is None:
             return None
         t1 = time.time()
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
+        time.sleep(0.25)  # let the sample covering the window's end arrive
         import datetime
         sm, smax, reasons, power = [], 0.0, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in list(self.lines):
             f = [c.strip() for c in line.split(",")]
             if len(f) < 10:
                 continue
@@ -179,6 +187,15 @@ class ClockSampler:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
                 "samples": len(sm), "power_w_max": max(power) if power else None}
+
+    def close(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.proc = None
 
 
 # ---------------------------------------------------------------------------
@@ -376,7 +393,7 @@ def bench_ours(args, dist):
         run_ours(seq, stream, lib)
 
     g = capture(fn)
-    clocks = ClockSampler(dist.device)
+    clocks = dist.clocks
     ms, clock_info = time_graph(g, args.steps, args.warmup, dist, clocks)
     tok_s = args.steps * dist.world / (ms / 1e3)
 
@@ -517,7 +534,7 @@ def bench_config0(args, dist):
                 raise RuntimeError(lib.gdsq_last_error().decode())
 
     g = capture(fn)
-    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dist.device))
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
     launches = args.steps * copies
     us = ms * 1e3 / launches
     b = gemv_alg_bytes(n, k, q4_bytes(n, k))
@@ -659,7 +676,7 @@ def bench_config3(args, dist):
         tdist.all_gather_into_tensor(logits, logits_local)
         torch.cuda.synchronize()
     g = capture(token)
-    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dev) if rank == 0 else None)
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
     del g
     tok_s = args.steps / (ms / 1e3)
     per_token_bytes = wbytes_rank * ws
@@ -729,7 +746,7 @@ def bench_config4(args, dist):
             x = x + (mods[l % NPHYS](x) if ws > 1 else moe.moe_mlp_decode(x, layer, TOPK))
     torch.cuda.synchronize()
     g = capture(step)
-    ms, clk = time_graph(g, args.steps, args.warmup, dist, ClockSampler(dev) if rank == 0 else None)
+    ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
     del g
     step_s = ms / args.steps / 1e3
     return {"metric": "Qwen-MoE-shaped affine-Q4 MoE decode tok/s, expert-parallel (60 layers x (router top-10 + "
@@ -761,7 +778,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    dist = Dist()
+    dist = Dist(sample_clocks=args.impl != "reference")
     try:
         if args.impl == "reference":
             res = bench_reference(args, dist)
