@@ -82,6 +82,21 @@ def gemv_affine_q4(words, scales, biases, x: torch.Tensor, n: int, k: int, group
     return out
 
 
+def gemv_group(fmt: str, weights, x: torch.Tensor, out_dims, k: int, outs=None):
+    """Several GGUF matrices sharing x (and K) in one launch:
+    [y_m [B, out_dims[m]]] = W_m . x."""
+    b = x.numel() // k
+    count = len(weights)
+    if outs is None:
+        outs = [torch.empty(b, n, dtype=torch.float16, device=x.device) for n in out_dims]
+    wa = (ctypes.c_void_p * count)(*[w.data_ptr() for w in weights])
+    ya = (ctypes.c_void_p * count)(*[y.data_ptr() for y in outs])
+    na = (ctypes.c_int * count)(*out_dims)
+    check(lib().gdsq_fused_gemv_group(0 if fmt == "q4_0" else 1, count, wa, na, ya, _p(x), k, b, _stream(x)),
+          "gdsq_fused_gemv_group")
+    return outs
+
+
 MOE_OUT_F32 = 1      # GDSQ_MOE_OUT_F32
 MOE_ACCUMULATE = 2   # GDSQ_MOE_ACCUMULATE
 MOE_CLAMP = 4        # GDSQ_MOE_CLAMP

@@ -330,8 +330,20 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
   return GDSQ_OK;
 }
 
+// `wlist` (host array of `p.count` weight pointers) for a grouped launch whose
+// rg_start / ys / ns the caller has filled; nullptr for a plain launch.
 template <int F, int B, int GS>
-int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
+int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream, const void* const* wlist = nullptr) {
+  if (wlist == nullptr) {
+    p.count = 1;
+    p.rg_start[0] = 0;
+    for (int m = 1; m <= kMaxGroup; ++m) p.rg_start[m] = (p.N + 31) / 32;
+    p.ys[0] = p.y;
+    p.ns[0] = p.N;
+  } else {
+    for (int m = p.count + 1; m <= kMaxGroup; ++m) p.rg_start[m] = p.rg_start[p.count];
+    p.N = p.rg_start[p.count] * 32;  // the planner sees the concatenated rows
+  }
   const uint64_t key = ((uint64_t)F << 60) | ((uint64_t)B << 54) | ((uint64_t)GS << 44) |
                        ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
   GemvPlan plan;
@@ -354,16 +366,20 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
       g_plans[dev.ordinal][key] = plan;
     }
   }
-  CUtensorMap wmap;
-  int mst = weight_map<F>(dev, p.w, p.N, p.row_bytes, &wmap);
-  if (mst != GDSQ_OK) return mst;
+  CUtensorMap maps[kMaxGroup];
+  for (int m = 0; m < p.count; ++m) {
+    const void* wm = wlist ? wlist[m] : p.w;
+    int mst = weight_map<F>(dev, wm, p.ns[m], p.row_bytes, &maps[m]);
+    if (mst != GDSQ_OK) return mst;
+  }
+  for (int m = p.count; m < kMaxGroup; ++m) maps[m] = maps[0];
   auto kernel = gemv_fast_kernel<F, B, GS>;
   cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
   p.cs = plan.cs;
   p.stages = plan.stages;
   p.copy = plan.copy;
-  p.num_rg = (p.N + 31) / 32;
+  p.num_rg = p.rg_start[p.count];
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.nclusters * plan.cs);
@@ -386,9 +402,19 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
+  e = cudaLaunchKernelEx(&cfg, kernel, p, maps[0], maps[1], maps[2], maps[3]);
   if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
   return GDSQ_OK;
+}
+
+template <int F>
+int launch_fast_group(const GemvParams& p, const DeviceInfo& dev, cudaStream_t stream, const void* const* wl) {
+  switch (batch_tile(p.nb)) {
+    case 1: return launch_fast<F, 1, 0>(p, dev, stream, wl);
+    case 2: return launch_fast<F, 2, 0>(p, dev, stream, wl);
+    case 3: return launch_fast<F, 3, 0>(p, dev, stream, wl);
+    default: return launch_fast<F, 4, 0>(p, dev, stream, wl);
+  }
 }
 
 template <int F, int GS>
@@ -1133,6 +1159,56 @@ int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void
                               int batch, void* stream) {
   return gemv_dispatch(kFmtAffineQ4, weight, scales, biases, x, y, out_dim, in_dim, group_size,
                        batch, stream);
+}
+
+int gdsq_fused_gemv_group(int gguf_type, int count, const void* const* weights, const int* out_dims,
+                          void* const* ys, const void* x, int in_dim, int batch, void* stream_v) {
+  t_last_error.clear();
+  if (gguf_type != GDSQ_TYPE_Q4_0 && gguf_type != GDSQ_TYPE_Q8_0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "gemv group: gguf_type %d is neither Q4_0 nor Q8_0", gguf_type);
+  if (count < 1 || count > kMaxGroup || !weights || !out_dims || !ys)
+    return fail(GDSQ_ERR_INVALID_VALUE, "gemv group: count %d outside 1..%d or null arrays", count, kMaxGroup);
+  const int fmt = gguf_type == GDSQ_TYPE_Q4_0 ? kFmtQ4_0 : kFmtQ8_0;
+  bool fast = batch >= 1 && batch <= 4 && in_dim > 0 && in_dim % kChunkCols == 0 && x && aligned(x, 16);
+  for (int m = 0; m < count; ++m) {
+    if (out_dims[m] < 0) return fail(GDSQ_ERR_INVALID_VALUE, "gemv group: negative out_dim %d", out_dims[m]);
+    fast = fast && weights[m] && aligned(weights[m], 16) && out_dims[m] > 0 && ys[m] && aligned(ys[m], 2);
+  }
+  if (count == 1 || !fast || tcb_mode() == 1) {
+    // One launch per matrix (every check and path of the single GEMV).
+    for (int m = 0; m < count; ++m) {
+      const int st = gemv_dispatch(fmt, weights[m], nullptr, nullptr, x, ys[m], out_dims[m], in_dim, 0, batch,
+                                   stream_v);
+      if (st != GDSQ_OK) return st;
+    }
+    return GDSQ_OK;
+  }
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  GemvParams p = {};
+  p.x = static_cast<const __half*>(x);
+  p.K = in_dim;
+  p.nb = batch;
+  p.row_bytes = fmt == kFmtQ4_0 ? (long long)in_dim / 32 * 18 : (long long)in_dim / 32 * 34;
+  p.count = count;
+  p.rg_start[0] = 0;
+  for (int m = 0; m < count; ++m) {
+    p.ys[m] = static_cast<__half*>(ys[m]);
+    p.ns[m] = out_dims[m];
+    p.rg_start[m + 1] = p.rg_start[m] + (out_dims[m] + 31) / 32;
+  }
+  p.w = static_cast<const uint8_t*>(weights[0]);
+  p.y = p.ys[0];
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (fmt == kFmtQ4_0) {
+    if (fast_min_smem<kFmtQ4_0>(batch, in_dim, 0) > dev->smem_optin)
+      return fail(GDSQ_ERR_UNSUPPORTED, "gemv group: no plan fits shared memory");
+    return launch_fast_group<kFmtQ4_0>(p, *dev, stream, weights);
+  }
+  if (fast_min_smem<kFmtQ8_0>(batch, in_dim, 0) > dev->smem_optin)
+    return fail(GDSQ_ERR_UNSUPPORTED, "gemv group: no plan fits shared memory");
+  return launch_fast_group<kFmtQ8_0>(p, *dev, stream, weights);
 }
 
 int gdsq_moe_affine_q4_gate_up(const void* gate_weight, const void* gate_scales, const void* gate_biases,

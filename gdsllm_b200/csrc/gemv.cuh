@@ -97,8 +97,18 @@ struct GemvParams {
   int cs;                 // CTAs per cluster (K slices)
   int stages;             // ring stages per warp (1..kMaxStages)
   int copy;               // chunks per ring stage (1..kMaxCopyChunks)
-  int num_rg;             // row groups = ceil(N / 32)
+  int num_rg;             // row groups = ceil(N / 32) (summed over the group)
+  // Grouped launch (GGUF formats): up to 4 matrices with the same K and x,
+  // their 32-row groups laid end to end; matrix m owns row groups
+  // [rg_start[m], rg_start[m + 1]), writes ys[m] and has ns[m] rows.
+  // count == 1 for a plain launch (ys[0] = y, ns[0] = N).
+  int count;
+  int rg_start[5];
+  __half* ys[4];
+  int ns[4];
 };
+
+constexpr int kMaxGroup = 4;
 
 // Shared-memory carve-up of the fast kernel, identical on host and device.
 struct GemvSmemLayout {
@@ -441,7 +451,9 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
 
 template <int F, int B, int GS>
 __global__ void __launch_bounds__(kGemvWarps * 32)
-    gemv_fast_kernel(const GemvParams p, const __grid_constant__ CUtensorMap wmap) {
+    gemv_fast_kernel(const GemvParams p, const __grid_constant__ CUtensorMap wmap,
+                     const __grid_constant__ CUtensorMap wmap1, const __grid_constant__ CUtensorMap wmap2,
+                     const __grid_constant__ CUtensorMap wmap3) {
   using T = GemvFormat<F>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // TMA destinations (the 128-byte swizzle in particular) need a 1024-byte
@@ -483,22 +495,37 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
-    if (warp == 0) prefetch_tensor_map(&wmap);
+    if (warp == 0) {
+      prefetch_tensor_map(&wmap);
+      if (p.count > 1) prefetch_tensor_map(&wmap1);
+      if (p.count > 2) prefetch_tensor_map(&wmap2);
+      if (p.count > 3) prefetch_tensor_map(&wmap3);
+    }
   }
   __syncwarp();
   if (cs > 1) cluster_arrive_relaxed();  // waited for before the first DSMEM store
+
+  // Matrix of a global row group and the group's first row inside it.
+  auto locate = [&](int rg, int* m, int* lrow0) {
+    int mm = 0;
+    if (p.count > 1) mm = (rg >= p.rg_start[1]) + (rg >= p.rg_start[2]) + (rg >= p.rg_start[3]);
+    *m = mm;
+    *lrow0 = (rg - p.rg_start[mm]) * 32;
+  };
 
   // Producer cursor: the next (item, step) to copy and the stage it goes to.
   int p_item = 0, p_step = 0, p_stage = 0, issued = 0;
   auto issue_next = [&]() {
     if (lane == 0) {
-      const int row0 = (cluster + p_item * nclusters) * 32;
+      int m, row0;
+      locate(cluster + p_item * nclusters, &m, &row0);
+      const CUtensorMap* map = m == 0 ? &wmap : m == 1 ? &wmap1 : m == 2 ? &wmap2 : &wmap3;
       const int chunk = c0 + wc0 + p_step * CP;
       const int nch = min(CP, mw - p_step * CP);
       uint8_t* dst = ring + p_stage * stage_bytes<F>(CP);
       mbar_arrive_expect_tx(&bars[p_stage], static_cast<uint32_t>(nch * 32 * T::kChunkBytes));
       for (int j = 0; j < nch; ++j)
-        tma_load_2d(dst + j * (32 * T::kChunkBytes), &wmap, (chunk + j) * (T::kChunkBytes / 8), row0,
+        tma_load_2d(dst + j * (32 * T::kChunkBytes), map, (chunk + j) * (T::kChunkBytes / 8), row0,
                     &bars[p_stage], policy);
     }
     ++issued;
@@ -548,8 +575,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   int stage = 0;
   uint32_t phase = 0;
   for (int item = 0; item < nitems; ++item) {
-    const int row0 = (cluster + item * nclusters) * 32;
-    const int nvalid = min(32, p.N - row0);
+    int m, row0;
+    locate(cluster + item * nclusters, &m, &row0);
+    const int Nm = p.ns[m];
+    __half* ym = p.ys[m];
+    const int nvalid = min(32, Nm - row0);
     if (F == kFmtAffineQ4 && item > 0) {
       __syncthreads();
       load_sb(row0);
@@ -609,7 +639,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 #pragma unroll
       for (int wv = 0; wv < kGemvWarps; ++wv) v += rd[(wv * B + b) * 32 + l];
       if (cs == 1) {
-        if (b < p.nb && l < nvalid) p.y[(size_t)b * p.N + row0 + l] = __float2half_rn(v);
+        if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
       } else {
         st_cluster_f32(map_to_rank(sl + (crank * B + b) * 32 + l, 0), v);
       }
@@ -623,7 +653,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
           if (b < p.nb && l < nvalid) {
             float v = 0.f;
             for (int r = 0; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
-            p.y[(size_t)b * p.N + row0 + l] = __float2half_rn(v);
+            ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
           }
         }
       }

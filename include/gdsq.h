@@ -106,6 +106,18 @@ GDSQ_API int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, c
                               const void* x, void* y, int out_dim, int in_dim, int group_size,
                               int batch, void* stream);
 
+/* Several GGUF matrices that read the same x (LLaMA's q, k, v; gate, up) in
+ * one launch: ys[m][b][n] = fp16( sum_k W_m[n][k] * x[b][k] ).  Host arrays
+ * `weights`, `out_dims`, `ys` of `count` (1..4) entries; gguf_type
+ * GDSQ_TYPE_Q4_0 or GDSQ_TYPE_Q8_0.  No single reference launcher: the
+ * reference calls launch_fused_*_gemv once per matrix (llama.py:122-141).
+ * Shapes the fast path cannot take (in_dim % 256, alignment, batch > 4) run
+ * as one launch per matrix with the same results. */
+#define GDSQ_TYPE_Q4_0 0
+#define GDSQ_TYPE_Q8_0 1
+GDSQ_API int gdsq_fused_gemv_group(int gguf_type, int count, const void* const* weights, const int* out_dims,
+                                   void* const* ys, const void* x, int in_dim, int batch, void* stream);
+
 /* ---- Mixture-of-experts gather (affine-Q4 experts, decode) ------------- */
 
 /* No single reference launcher: these two calls replace the decode loop of

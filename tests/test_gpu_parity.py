@@ -289,3 +289,30 @@ def test_gemv_batched_paths_agree(gdsq, cuda, monkeypatch):
     torch.cuda.synchronize()
     _check_gemv(y_cc, w16, x, "cuda cores")
     _check_gemv(y_tc, w16, x, "tensor cores")
+
+
+# ---- grouped launch: matrices sharing x (q/k/v, gate/up) ---------------------
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("dims,k", [((4096, 4096, 4096), 4096), ((4096, 1024, 1024), 8192), ((11008, 11008), 4096),
+                                    ((100, 33, 300, 64), 1024), ((96, 40), 96)])
+@pytest.mark.parametrize("batch", [1, 3, 8])
+def test_gemv_group(gdsq, cuda, fmt, dims, k, batch):
+    """Each output of one grouped launch meets the GEMV bar of its own matrix
+    (K = 96 and batch 8 run as one launch per matrix)."""
+    make, deq = (synth.q4_0_weight, oracle.dequant_q4_0) if fmt == "q4_0" else (synth.q8_0_weight, oracle.dequant_q8_0)
+    ws = [make(n, k, seed=11 * i + n) for i, n in enumerate(dims)]
+    x = synth.activations(batch, k, seed=len(dims) + batch).to(cuda)
+    ys = gdsq.gemv_group(fmt, [w.to(cuda) for w in ws], x, list(dims), k)
+    torch.cuda.synchronize()
+    for i, (w, y) in enumerate(zip(ws, ys)):
+        _check_gemv(y, deq(w.numpy()).reshape(dims[i], k), x, f"group {fmt} m{i} {dims[i]}x{k} b{batch}")
+    assert gdsq.device_error(0, clear=True) == 0
+
+
+def test_gemv_group_validation(gdsq, cuda):
+    from gdsllm_b200 import GdsqError
+    w = synth.q4_0_weight(64, 256).to(cuda)
+    x = synth.activations(1, 256).to(cuda)
+    with pytest.raises(GdsqError, match="count"):
+        gdsq.gemv_group("q4_0", [w] * 5, x, [64] * 5, 256)
