@@ -268,7 +268,7 @@ bool plan_override(int* cs, int* stages, int* copy) {
 // warps per SM are taken as enough to hide latency).  Candidates whose
 // shared memory does not fit are skipped.
 template <int F, int B, int GS>
-int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
+int make_plan_model(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
   using T = GemvFormat<F>;
   auto kernel = gemv_fast_kernel<F, B, GS>;
   const int R = (N + 31) / 32;
@@ -328,6 +328,57 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
   }
   if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no GEMV launch plan fits shared memory");
   return GDSQ_OK;
+}
+
+// Batch 1 (the decode chain): measured on B200 over the decode shapes in
+// dependent launch chains with programmatic dependent launch (4096x4096,
+// 12288x4096 and 22016x4096 grouped, 4096x11008), the fastest plans used the
+// smallest cluster split giving a few CTAs per SM, at most 4 CTAs per
+// cluster, two ring stages and one chunk per stage; wider splits pay a
+// cluster reduction per row group, deeper rings only take shared memory
+// from co-resident CTAs of the next launch.  Rule: the smallest power of two
+// cs <= 4 with R * cs >= 4 * SMs, then fewer stages or a wider split if
+// shared memory does not fit.  Batches > 1 keep the cost model above (their
+// staged activations make shared memory, hence occupancy, the constraint).
+template <int F, int B, int GS>
+int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
+  if (B > 1) return make_plan_model<F, B, GS>(N, K, dev, out);
+  auto kernel = gemv_fast_kernel<F, B, GS>;
+  const int R = (N + 31) / 32;
+  const int C = K / kChunkCols;
+  int force_cs = 0, force_st = 0, force_cp = 0;
+  const bool forced = plan_override(&force_cs, &force_st, &force_cp);
+  int want_cs = 1;
+  while (want_cs < 4 && want_cs * 2 <= C && (long long)R * want_cs < 4LL * dev.sms) want_cs *= 2;
+  struct Cand { int cs, st, cp; };
+  Cand cands[16];
+  int nc = 0;
+  if (forced) {
+    cands[nc++] = {force_cs, force_st, force_cp ? force_cp : 1};
+  } else {
+    for (int cs = want_cs; cs <= kMaxCluster && cs <= C; cs *= 2)
+      for (int st = 2; st >= 1; --st) cands[nc++] = {cs, st, 1};
+  }
+  for (int i = 0; i < nc; ++i) {
+    const Cand c = cands[i];
+    if (c.cs > C || c.cp > GemvFormat<F>::kMaxCopyChunks) continue;
+    const GemvSmemLayout L = gemv_smem_layout<F>(B, K, GS, c.cs, c.st, c.cp);
+    if (L.total > dev.smem_optin) continue;
+    cudaError_t e = ensure_smem(kernel, L.total, dev.ordinal);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, L.total);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (occ < 1) continue;
+    const long long slots = (long long)dev.sms * occ;
+    out->cs = c.cs;
+    out->stages = c.st;
+    out->copy = c.cp;
+    out->nclusters = (long long)R * c.cs <= slots ? R : (int)(slots / c.cs);
+    out->smem = L.total;
+    return GDSQ_OK;
+  }
+  return fail(GDSQ_ERR_UNSUPPORTED, "no GEMV launch plan fits shared memory");
 }
 
 // `wlist` (host array of `p.count` weight pointers) for a grouped launch whose
