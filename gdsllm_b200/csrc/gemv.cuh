@@ -492,8 +492,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   const uint32_t ring_a = smem_addr(ring) + lane * T::kChunkBytes;  // this lane's row, stage 0, chunk 0
   const uint64_t policy = l2_policy_evict_first();
 
+  // Cluster reduction barriers (after the per-warp stage barriers): the
+  // leader's red_full[item & 1] counts the peers' partial-sum stores, a
+  // peer's red_empty[item & 1] the leader's release of that slot buffer.
+  uint64_t* red_full = reinterpret_cast<uint64_t*>(smem) + kGemvWarps * kMaxStages;
+  uint64_t* red_empty = red_full + 2;
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    if (warp == 0 && cs > 1) {
+      for (int d = 0; d < 2; ++d) {
+        mbar_init(&red_full[d], (cs - 1) * B * 32);
+        mbar_init(&red_empty[d], B * 32);
+      }
+    }
     fence_barrier_init();
     if (warp == 0) {
       prefetch_tensor_map(&wmap);
@@ -631,8 +642,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     for (int b = 0; b < B; ++b) rd[(warp * B + b) * 32 + lane] = acc[b];
     if (cs > 1 && item == 0) cluster_wait();  // every peer is running: DSMEM stores are safe
     __syncthreads();
+    // Peers push their partial sums into the leader's slot buffer and arrive
+    // on its barrier; only the leader waits (no cluster-wide barrier).
     float* sl = slots + (item & 1) * (cs * B * 32);
-    for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {
+    const uint32_t par = (item >> 1) & 1;
+    for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {  // one arrival per (b, l)
       const int b = idx >> 5;
       const int l = idx & 31;
       float v = 0.f;
@@ -640,21 +654,22 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       for (int wv = 0; wv < kGemvWarps; ++wv) v += rd[(wv * B + b) * 32 + l];
       if (cs == 1) {
         if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
-      } else {
+      } else if (crank != 0) {
+        if (item >= 2 && ok && !mbar_wait_cluster(&red_empty[item & 1], par ^ 1)) {
+          ok = false;
+          record_device_error(kDevErrBarrierTimeout);
+        }
         st_cluster_f32(map_to_rank(sl + (crank * B + b) * 32 + l, 0), v);
-      }
-    }
-    if (cs > 1) {
-      cluster_sync_all();
-      if (crank == 0) {
-        for (int idx = threadIdx.x; idx < B * 32; idx += blockDim.x) {
-          const int b = idx >> 5;
-          const int l = idx & 31;
-          if (b < p.nb && l < nvalid) {
-            float v = 0.f;
-            for (int r = 0; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
-            ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
-          }
+        mbar_arrive_cluster(map_to_rank(&red_full[item & 1], 0));
+      } else {
+        if (ok && !mbar_wait_cluster(&red_full[item & 1], par)) {
+          ok = false;
+          record_device_error(kDevErrBarrierTimeout);
+        }
+        for (int r = 1; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
+        if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
+        if (item + 2 < nitems) {
+          for (int r = 1; r < cs; ++r) mbar_arrive_cluster(map_to_rank(&red_empty[item & 1], r));
         }
       }
     }

@@ -316,3 +316,20 @@ def test_gemv_group_validation(gdsq, cuda):
     x = synth.activations(1, 256).to(cuda)
     with pytest.raises(GdsqError, match="count"):
         gdsq.gemv_group("q4_0", [w] * 5, x, [64] * 5, 256)
+
+
+@pytest.mark.parametrize("plan", ["1:2:1", "2:1:1", "4:2:1", "8:1:1", "8:2:1"])
+@pytest.mark.parametrize("fmt,batch", [("q4_0", 1), ("q8_0", 3), ("q4_0", 4)])
+def test_gemv_cuda_core_launch_plans(gdsq, cuda, plan, fmt, batch, monkeypatch):
+    """Every cluster split of the CUDA-core kernel, with many row groups per
+    cluster (32000 rows), so the cluster's partial-sum buffers are reused
+    and released item after item."""
+    monkeypatch.setenv("GDSQ_GEMV_TCB", "0")
+    monkeypatch.setenv("GDSQ_GEMV_PLAN", plan)
+    n, k = 32000, 4096
+    ws, w16 = _weights(fmt, n, k, 0, seed=17)
+    x = synth.activations(batch, k, seed=18).to(cuda)
+    y = _run(gdsq, fmt, ws, x, n, k, 0)
+    torch.cuda.synchronize()
+    _check_gemv(y, w16, x, f"cuda-core plan {plan} {fmt} b{batch}")
+    assert gdsq.device_error(0, clear=True) == 0
