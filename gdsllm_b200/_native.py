@@ -37,6 +37,7 @@ _C_SIGNATURES = {
     "gdsq_fused_gemv_group": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                                              ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_void_p),
                                              ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "gdsq_moe_affine_q4_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 23 + [ctypes.c_int] * 9 + [ctypes.c_void_p]),
     "gdsq_moe_route": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p]),

@@ -1288,6 +1288,79 @@ int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales, co
                       expert_first, expert_count, expert_total, flags, stream);
 }
 
+}  // extern "C"
+
+namespace gdsq {
+namespace {
+// Fixed device-side intermediate for gdsq_moe_affine_q4_noalloc: 4 MiB of
+// fp16 in the library's own static device memory (one copy per device), so
+// that entry point allocates nothing.
+constexpr size_t kNoAllocHElems = 2u << 20;
+static __device__ __align__(256) __half g_moe_h_scratch[kNoAllocHElems];
+void* g_moe_h_addr[kMaxDevices];
+bool g_moe_h_ready[kMaxDevices];
+
+// Device address of the array on the current device, looked up once per
+// device (with that device current) and cached.
+int moe_h_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GDSQ_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  if (!g_moe_h_ready[dev]) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_moe_h_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(MoE scratch)");
+    g_moe_h_addr[dev] = addr;
+    g_moe_h_ready[dev] = true;
+  }
+  *out = g_moe_h_addr[dev];
+  return GDSQ_OK;
+}
+}  // namespace
+}  // namespace gdsq
+
+extern "C" {
+
+int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales, const void* gate_biases,
+                               const void* up_weight, const void* up_scales, const void* up_biases,
+                               const void* down_weight, const void* down_scales, const void* down_biases,
+                               const void* shared_gate_weight, const void* shared_gate_scales,
+                               const void* shared_gate_biases, const void* shared_up_weight,
+                               const void* shared_up_scales, const void* shared_up_biases,
+                               const void* shared_down_weight, const void* shared_down_scales,
+                               const void* shared_down_biases, const void* x, const int32_t* expert_ids,
+                               const void* route_weights, const void* shared_weights, void* y, int num_tokens,
+                               int top_k, int hidden_dim, int inter_dim, int group_size, int expert_first,
+                               int expert_count, int expert_total, int flags, void* stream) {
+  t_last_error.clear();
+  const bool shared = shared_gate_weight != nullptr;
+  const long long need = (long long)num_tokens * (top_k + (shared ? 1 : 0)) * inter_dim;
+  if (num_tokens < 0 || top_k < 1 || inter_dim <= 0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe noalloc: num_tokens %d, top_k %d, inter_dim %d", num_tokens, top_k,
+                inter_dim);
+  if (need > (long long)kNoAllocHElems)
+    return fail(GDSQ_ERR_INVALID_VALUE,
+                "moe noalloc: %d tokens x %d slots x %d intermediate = %lld fp16 exceeds the %zu-element "
+                "static scratch; use gdsq_moe_affine_q4_gate_up / _down with a caller buffer",
+                num_tokens, top_k + (shared ? 1 : 0), inter_dim, need, kNoAllocHElems);
+  if (num_tokens == 0) return GDSQ_OK;
+  void* h = nullptr;
+  int st = moe_h_scratch(&h);
+  if (st != GDSQ_OK) return st;
+  st = gdsq_moe_affine_q4_gate_up(gate_weight, gate_scales, gate_biases, up_weight, up_scales, up_biases,
+                                  shared_gate_weight, shared_gate_scales, shared_gate_biases, shared_up_weight,
+                                  shared_up_scales, shared_up_biases, x, expert_ids, h, num_tokens, top_k,
+                                  inter_dim, hidden_dim, group_size, expert_first, expert_count, expert_total,
+                                  stream);
+  if (st != GDSQ_OK) return st;
+  return gdsq_moe_affine_q4_down(down_weight, down_scales, down_biases, shared_down_weight, shared_down_scales,
+                                 shared_down_biases, h, expert_ids, route_weights, shared_weights, y, num_tokens,
+                                 top_k, hidden_dim, inter_dim, group_size, expert_first, expert_count,
+                                 expert_total, flags, stream);
+}
+
 int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,
                    const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
                    void* shared_weights, void* stream_v) {

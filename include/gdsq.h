@@ -167,6 +167,30 @@ GDSQ_API int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_s
                                      int hidden_dim, int inter_dim, int group_size, int expert_first,
                                      int expert_count, int expert_total, int flags, void* stream);
 
+/* gdsq_moe_affine_q4_gate_up then gdsq_moe_affine_q4_down (same arguments,
+ * same results) with the intermediate h kept in a fixed 4 MiB array of the
+ * library's static device memory instead of a caller buffer, so the call
+ * allocates nothing.  No reference counterpart.  Limits: num_tokens *
+ * (top_k + 1 if the shared expert is given, else top_k) * inter_dim <=
+ * 2097152 fp16 elements, otherwise GDSQ_ERR_INVALID_VALUE before any CUDA
+ * call.  The array is shared by every call on a device: calls on different
+ * streams (or host threads) at the same time overwrite each other's h, so
+ * serialise them or use the two-call form with your own buffer.  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress) and
+ * must happen before any stream capture that records a later call. */
+GDSQ_API int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales, const void* gate_biases,
+                                        const void* up_weight, const void* up_scales, const void* up_biases,
+                                        const void* down_weight, const void* down_scales, const void* down_biases,
+                                        const void* shared_gate_weight, const void* shared_gate_scales,
+                                        const void* shared_gate_biases, const void* shared_up_weight,
+                                        const void* shared_up_scales, const void* shared_up_biases,
+                                        const void* shared_down_weight, const void* shared_down_scales,
+                                        const void* shared_down_biases, const void* x, const int32_t* expert_ids,
+                                        const void* route_weights, const void* shared_weights, void* y,
+                                        int num_tokens, int top_k, int hidden_dim, int inter_dim, int group_size,
+                                        int expert_first, int expert_count, int expert_total, int flags,
+                                        void* stream);
+
 /* The routing tail of moe_route (qwen_moe.py:407-413) on router logits fp16
  * [num_tokens][num_experts] (the output of F.linear(x, W_router)): expert_ids
  * int32 [num_tokens][top_k] of the top_k largest logits, largest first (equal
