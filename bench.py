@@ -752,7 +752,8 @@ def bench_config4(args, dist):
     from gdsllm_b200 import capi, ep, moe
     peak, peak_kind = load_peaks()
     capi.set_pdl(bool(args.pdl))
-    E, H, I, G, TOPK, NL, NPHYS = 512, 4096, 1024, 128, 10, 60, 8
+    E, H, I, G, TOPK, NL = args.experts, 4096, 1024, 128, 10, 60
+    NPHYS = args.resident_layers
     ws, rank, dev = dist.world, dist.rank, dist.device
     B = args.batch
     first, count = ep.expert_range(rank, ws, E)
@@ -799,7 +800,7 @@ def bench_config4(args, dist):
             "value": round(B / step_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random affine-Q4 experts, config 4 shapes)",
-            "config": {"workload": f"config 4: 512 experts + shared, hidden 4096, expert intermediate 1024, top-10, "
+            "config": {"workload": f"config 4: {E} experts + shared, hidden 4096, expert intermediate 1024, top-10, "
                                    f"batch {B}, 60 layers cycling {NPHYS} resident layers",
                        "parallelism": f"ep{ws}", "experts_per_gpu": count,
                        "touched_weight_gb_per_step": round(touched / 1e9, 3),
@@ -818,6 +819,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--batch", type=int, default=1, help="config 4: tokens per decode step (1 or 8)")
+    ap.add_argument("--resident-layers", type=int, default=8,
+                    help="config 4: distinct MoE layers held on the GPU and cycled over the 60 (3.4 GB each; "
+                         "8 by default, fewer only for profiler captures)")
+    ap.add_argument("--experts", type=int, default=512,
+                    help="config 4: experts per layer (512; fewer only for profiler captures -- the per-token "
+                         "work, 10 routed + 1 shared expert per layer, is the same)")
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
