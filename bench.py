@@ -705,12 +705,12 @@ def bench_config3(args, dist):
                     gemv("q4_0", wl[name], x, buf[name], n, k, stream)
             gemv("q4_0", wl["o"], buf["q"], o_out, H, Q // ws, stream)   # attention output stands in as q's shard
             if ws > 1:
-                tdist.all_reduce(o_out)
+                allreduce(o_out)
             gemv("q4_0", wl["gate"], o_out, buf["gate"], FF // ws, H, stream)
             gemv("q4_0", wl["up"], o_out, buf["up"], FF // ws, H, stream)
             gemv("q4_0", wl["down"], buf["up"], d_out, H, FF // ws, stream)
             if ws > 1:
-                tdist.all_reduce(d_out)
+                allreduce(d_out)
             x = d_out
         gemv("q8_0", lm, x, logits_local, V // ws, H, stream)
         if ws > 1:
@@ -720,20 +720,34 @@ def bench_config3(args, dist):
         tdist.all_reduce(o_out)
         tdist.all_gather_into_tensor(logits, logits_local)
         torch.cuda.synchronize()
+    peer = None
+    if ws > 1 and args.tp_allreduce == "p2p":
+        from gdsllm_b200.p2p import PeerAllReduce
+        peer = PeerAllReduce(H, device=dev)
+
+    def allreduce(t):
+        if peer is not None:
+            peer(t)
+        else:
+            tdist.all_reduce(t)
     g = capture(token)
     ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
     del g
+    if peer is not None:
+        peer.close()
     tok_s = args.steps / (ms / 1e3)
     per_token_bytes = wbytes_rank * ws
     launches = args.steps * (NL * 7 + 1)
     return {"metric": "LLaMA-70B-shaped Q4_0 batch-1 decode tok/s, tensor-parallel GEMV chain (560 Q4_0 "
-                      "projections + Q8_0 lm_head per token, NCCL all-reduce after o and down)",
+                      "projections + Q8_0 lm_head per token, all-reduce after o and down)",
             "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random Q4_0/Q8_0 shards, config 3 shapes)",
             "config": {"workload": "config 3: 80 layers, hidden 8192, q 8192 / kv 1024 rows, FFN 28672, vocab 32000 "
                                    "(Q8_0 lm_head), batch 1; attention and norms are not on the path",
                        "parallelism": f"tp{ws}", "weights_per_gpu_gb": round(wbytes_rank / 1e9, 2),
+                       "allreduce": ("one-shot over NVLink peer memory (gdsq_allreduce_sum_f16)"
+                                     if peer is not None else "NCCL") if ws > 1 else None,
                        "l2": "every token streams 38.5 GB / N per GPU (> L2)"},
             "roofline": {"bound": "hbm", "achieved": round(wbytes_rank / (ms / args.steps / 1e3) / 1e9, 1),
                          "peak": peak, "unit": "GB/s",
@@ -819,6 +833,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--batch", type=int, default=1, help="config 4: tokens per decode step (1 or 8)")
+    ap.add_argument("--tp-allreduce", choices=["p2p", "nccl"], default="p2p",
+                    help="config 3: the o/down all-reduce, over peer memory (default) or NCCL")
     ap.add_argument("--resident-layers", type=int, default=8,
                     help="config 4: distinct MoE layers held on the GPU and cycled over the 60 (3.4 GB each; "
                          "8 by default, fewer only for profiler captures)")

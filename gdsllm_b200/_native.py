@@ -38,6 +38,9 @@ _C_SIGNATURES = {
                                              ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_void_p),
                                              ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "gdsq_moe_affine_q4_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 23 + [ctypes.c_int] * 9 + [ctypes.c_void_p]),
+    "gdsq_allreduce_sum_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                              ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "gdsq_moe_route": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p]),

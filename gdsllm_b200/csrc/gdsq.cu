@@ -21,6 +21,7 @@
 #include "gemv_tc.cuh"
 #include "gemv_tcb.cuh"
 #include "moe.cuh"
+#include "p2p.cuh"
 
 namespace gdsq {
 namespace {
@@ -1359,6 +1360,37 @@ int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales,
                                  shared_down_biases, h, expert_ids, route_weights, shared_weights, y, num_tokens,
                                  top_k, hidden_dim, inter_dim, group_size, expert_first, expert_count,
                                  expert_total, flags, stream);
+}
+
+int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* bufs, void* const* flags, int cap,
+                           int rank, int world, void* stream_v) {
+  t_last_error.clear();
+  if (world < 1 || world > kP2PMaxRanks || rank < 0 || rank >= world)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce: rank %d of world %d (at most %d ranks)", rank, world, kP2PMaxRanks);
+  if (n < 0 || n % 8 != 0 || n > cap || (n + kP2PElemsPerCta - 1) / kP2PElemsPerCta > kP2PMaxCtas)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce: n %d must be a multiple of 8, <= capacity %d and <= %d", n, cap,
+                kP2PMaxCtas * kP2PElemsPerCta);
+  if (n == 0) return GDSQ_OK;
+  if (!in || !out || !bufs || !flags) return fail(GDSQ_ERR_INVALID_VALUE, "allreduce: null pointer");
+  P2PArgs a = {};
+  a.in = static_cast<const __half*>(in);
+  a.out = static_cast<__half*>(out);
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !flags[r] || !aligned(bufs[r], 16) || !aligned(flags[r], 4))
+      return fail(GDSQ_ERR_MISALIGNED, "allreduce: rank %d buffer must be 16-byte aligned and non-null", r);
+    a.bufs[r] = static_cast<__half*>(const_cast<void*>(bufs[r]));
+    a.flags[r] = static_cast<int*>(flags[r]);
+  }
+  if (!aligned(in, 16) || !aligned(out, 16))
+    return fail(GDSQ_ERR_MISALIGNED, "allreduce: input and output must be 16-byte aligned");
+  a.n = n;
+  a.cap = cap;
+  a.rank = rank;
+  a.world = world;
+  const int grid = (n + kP2PElemsPerCta - 1) / kP2PElemsPerCta;
+  cudaError_t e = launch(allreduce_oneshot_kernel, dim3(grid), dim3(kP2PThreads), 0,
+                         static_cast<cudaStream_t>(stream_v), g_pdl_enabled != 0, a);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "allreduce launch");
 }
 
 int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,

@@ -191,6 +191,20 @@ GDSQ_API int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gat
                                         int expert_first, int expert_count, int expert_total, int flags,
                                         void* stream);
 
+/* ---- Tensor-parallel exchange ----------------------------------------- */
+
+/* out[i] = sum over ranks r (in rank order, fp32) of in_r[i], fp16, over
+ * NVLink peer memory: a one-shot all-reduce for the row-split projections'
+ * partial outputs (no reference counterpart: the reference runs one GPU).
+ * bufs / flags: host arrays of `world` device pointers, entry r = rank r's
+ * data buffer (2 * cap fp16, 16-byte aligned) and flag array (32 * 8 int32,
+ * zero-initialised), mapped into this process (CUDA IPC); entry `rank` is
+ * this rank's own.  Every rank must make the same sequence of calls.  n %
+ * 8 == 0, n <= cap, n <= 32768.  A peer that does not arrive within 1 s sets
+ * device error bit 1 and the call returns without a result. */
+GDSQ_API int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* bufs, void* const* flags,
+                                    int cap, int rank, int world, void* stream);
+
 /* The routing tail of moe_route (qwen_moe.py:407-413) on router logits fp16
  * [num_tokens][num_experts] (the output of F.linear(x, W_router)): expert_ids
  * int32 [num_tokens][top_k] of the top_k largest logits, largest first (equal

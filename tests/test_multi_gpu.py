@@ -71,7 +71,39 @@ def _worker(rank, world, port, q):
         y_ref = capi.gemv_q4_0(wt, xk, k, n)
         res["row"] = (y_row.float() - y_ref.float()).abs().max().item()
         res["row_scale"] = y_ref.float().abs().max().item()
+        # ---- one-shot all-reduce over peer memory vs NCCL ----
+        from gdsllm_b200.p2p import PeerAllReduce
+        ar = PeerAllReduce(32768)
+        worst = 0.0
+        for it, n in enumerate([8192, 1024, 24576, 8192, 8192]):
+            t = synth.activations(1, n, seed=100 * it + rank).to(dev).view(-1)
+            ref = t.clone()
+            dist.all_reduce(ref)
+            out = ar(t.clone())
+            worst = max(worst, ((out.float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
+        # inside a CUDA graph, replayed with new inputs (device-side epochs)
+        gin = torch.empty(8192, dtype=torch.float16, device=dev)
+        gout = torch.empty_like(gin)
+        s0 = torch.cuda.Stream()
+        s0.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s0):
+            ar(gin.copy_(synth.activations(1, 8192, seed=1).view(-1).to(dev)), out=gout)
+        torch.cuda.current_stream().wait_stream(s0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ar(gin, out=gout)
+        for it in range(5):
+            gin.copy_(synth.activations(1, 8192, seed=50 + it + 10 * rank).view(-1).to(dev))
+            g.replay()
+            ref = gin.clone()
+            dist.all_reduce(ref)
+            torch.cuda.synchronize()
+            worst = max(worst, ((gout.float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
+        del g
+        res["p2p"] = worst
+        res["p2p_err"] = capi.device_error(rank, clear=True)
         torch.cuda.synchronize()
+        ar.close()
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -98,3 +130,6 @@ def test_expert_and_tensor_parallel_on_two_gpus():
         assert res["col"] <= 2e-3 * res["col_scale"] + 1e-3, (rank, res)
         # row split: two fp16 partials added (one extra rounding each)
         assert res["row"] <= 4e-3 * res["row_scale"] + 2e-3, (rank, res)
+        # peer all-reduce: fp32 sum vs NCCL's fp16 sum, relative to the value
+        assert res["p2p"] <= 2e-3, (rank, res)
+        assert res["p2p_err"] == 0, (rank, res)
