@@ -3,8 +3,8 @@
 The reference kernels are compiled unchanged from the reference tree into
 oracle/_ref/libref_kernels.so (python oracle/build.py, in a container that
 has the tree); this script runs them on seeded inputs and writes
-``ref_kernels.npz`` (default: gpurun_out/ref_kernels.npz, then committed as
-tests/golden/ref_kernels.npz).  tests/test_oracle.py checks the CPU oracle
+``ref_kernels.npz`` (default: tests/golden/ref_kernels.npz, the committed
+fixture).  tests/test_oracle.py checks the CPU oracle
 against these outputs: dequantized values bit for bit, GEMV outputs within
 the bar.
 
@@ -64,4 +64,4 @@ def main(out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else str(ROOT / "gpurun_out" / "ref_kernels.npz"))
+    main(sys.argv[1] if len(sys.argv) > 1 else str(ROOT / "tests" / "golden" / "ref_kernels.npz"))

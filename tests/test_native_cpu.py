@@ -100,6 +100,56 @@ def test_misaligned_pointers_are_rejected(call):
     assert call(lib()) == 2
 
 
+def _arr(ctype, vals):
+    import ctypes
+    return (ctype * len(vals))(*vals)
+
+
+def _moe_gate_up(l, top_k=4, group=128, first=0, count=8, total=8, shared=None):
+    sh = shared if shared is not None else [None] * 6
+    return l.gdsq_moe_affine_q4_gate_up(*([FAKE] * 6), *sh, FAKE, FAKE, FAKE, 1, top_k, 512, 1024, group, first, count,
+                                        total, None)
+
+
+@pytest.mark.parametrize("call,fragment", [
+    (lambda l: l.gdsq_fused_gemv_group(7, 2, _arr(ctypes_vp(), [FAKE, FAKE]), _arr(ctypes_int(), [8, 8]),
+                                       _arr(ctypes_vp(), [FAKE, FAKE]), FAKE, 256, 1, None), b"gguf_type"),
+    (lambda l: l.gdsq_fused_gemv_group(0, 5, _arr(ctypes_vp(), [FAKE] * 5), _arr(ctypes_int(), [8] * 5),
+                                       _arr(ctypes_vp(), [FAKE] * 5), FAKE, 256, 1, None), b"count 5"),
+    (lambda l: _moe_gate_up(l, top_k=65), b"top_k"),
+    (lambda l: _moe_gate_up(l, group=12), b"group_size"),
+    (lambda l: _moe_gate_up(l, first=4, count=8, total=8), b"resident experts"),
+    (lambda l: _moe_gate_up(l, shared=[FAKE, None, None, None, None, None]), b"all given or all null"),
+    (lambda l: l.gdsq_moe_affine_q4_down(*([FAKE] * 3), None, None, None, FAKE, FAKE, FAKE, None, FAKE, 1, 4, 1024,
+                                         512, 128, 0, 8, 8, 8, None), b"unknown flags"),
+    (lambda l: l.gdsq_moe_route(FAKE, 1, 8, 9, None, None, 0, FAKE, FAKE, None, None), b"top_k"),
+    (lambda l: l.gdsq_moe_route(FAKE, 1, 5000, 10, None, None, 0, FAKE, FAKE, None, None), b"experts"),
+    (lambda l: l.gdsq_allreduce_sum_f16(FAKE, FAKE, 8192, _arr(ctypes_vp(), [FAKE] * 9),
+                                        _arr(ctypes_vp(), [FAKE] * 9), 8192, 0, 9, None), b"world 9"),
+    (lambda l: l.gdsq_allreduce_sum_f16(FAKE, FAKE, 12, _arr(ctypes_vp(), [FAKE, FAKE]),
+                                        _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 0, 2, None), b"multiple of 8"),
+    (lambda l: l.gdsq_allreduce_sum_f16(FAKE, FAKE, 16384, _arr(ctypes_vp(), [FAKE, FAKE]),
+                                        _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 1, 2, None), b"capacity"),
+])
+def test_invalid_arguments_of_the_additive_entry_points(call, fragment):
+    """The grouped GEMV, MoE and all-reduce entry points reject bad arguments
+    before any CUDA call."""
+    l = lib()
+    st = call(l)
+    assert st == 1, (st, l.gdsq_last_error())
+    assert fragment in l.gdsq_last_error(), l.gdsq_last_error()
+
+
+def ctypes_vp():
+    import ctypes
+    return ctypes.c_void_p
+
+
+def ctypes_int():
+    import ctypes
+    return ctypes.c_int
+
+
 def test_empty_work_is_a_no_op():
     l = lib()
     assert l.gdsq_dequant_q4_0(None, None, 0, None) == 0
