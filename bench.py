@@ -703,14 +703,20 @@ def bench_config3(args, dist):
             for name, (n, k) in cols.items():
                 if name in ("q", "k", "v"):
                     gemv("q4_0", wl[name], x, buf[name], n, k, stream)
-            gemv("q4_0", wl["o"], buf["q"], o_out, H, Q // ws, stream)   # attention output stands in as q's shard
-            if ws > 1:
-                allreduce(o_out)
+            if fused is not None:   # attention output stands in as q's shard
+                fused_row(wl["o"], buf["q"], o_out, H, Q // ws, stream)
+            else:
+                gemv("q4_0", wl["o"], buf["q"], o_out, H, Q // ws, stream)
+                if ws > 1:
+                    allreduce(o_out)
             gemv("q4_0", wl["gate"], o_out, buf["gate"], FF // ws, H, stream)
             gemv("q4_0", wl["up"], o_out, buf["up"], FF // ws, H, stream)
-            gemv("q4_0", wl["down"], buf["up"], d_out, H, FF // ws, stream)
-            if ws > 1:
-                allreduce(d_out)
+            if fused is not None:
+                fused_row(wl["down"], buf["up"], d_out, H, FF // ws, stream)
+            else:
+                gemv("q4_0", wl["down"], buf["up"], d_out, H, FF // ws, stream)
+                if ws > 1:
+                    allreduce(d_out)
             x = d_out
         gemv("q8_0", lm, x, logits_local, V // ws, H, stream)
         if ws > 1:
@@ -721,9 +727,19 @@ def bench_config3(args, dist):
         tdist.all_gather_into_tensor(logits, logits_local)
         torch.cuda.synchronize()
     peer = None
+    fused = None
     if ws > 1 and args.tp_allreduce == "p2p":
         from gdsllm_b200.p2p import PeerAllReduce
         peer = PeerAllReduce(H, device=dev)
+    if ws > 1 and args.tp_allreduce == "fused":
+        from gdsllm_b200.p2p import PeerRowGemv
+        fused = PeerRowGemv(H, device=dev)
+
+    def fused_row(w, x, y, n, k, stream):
+        st = lib.gdsq_fused_gemv_allreduce(0, w.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, fused.peer.bufs,
+                                           fused.peer.flags, fused.rows, fused.rank, fused.world, stream)
+        if st:
+            raise RuntimeError(lib.gdsq_last_error().decode())
 
     def allreduce(t):
         if peer is not None:
@@ -735,6 +751,8 @@ def bench_config3(args, dist):
     del g
     if peer is not None:
         peer.close()
+    if fused is not None:
+        fused.close()
     tok_s = args.steps / (ms / 1e3)
     per_token_bytes = wbytes_rank * ws
     launches = args.steps * (NL * 7 + 1)
@@ -746,7 +764,9 @@ def bench_config3(args, dist):
             "config": {"workload": "config 3: 80 layers, hidden 8192, q 8192 / kv 1024 rows, FFN 28672, vocab 32000 "
                                    "(Q8_0 lm_head), batch 1; attention and norms are not on the path",
                        "parallelism": f"tp{ws}", "weights_per_gpu_gb": round(wbytes_rank / 1e9, 2),
-                       "allreduce": ("one-shot over NVLink peer memory (gdsq_allreduce_sum_f16)"
+                       "allreduce": ("inside the row-split GEMV's epilogue over NVLink peer memory "
+                                     "(gdsq_fused_gemv_allreduce)" if fused is not None else
+                                     "one-shot over NVLink peer memory (gdsq_allreduce_sum_f16)"
                                      if peer is not None else "NCCL") if ws > 1 else None,
                        "l2": "every token streams 38.5 GB / N per GPU (> L2)"},
             "roofline": {"bound": "hbm", "achieved": round(wbytes_rank / (ms / args.steps / 1e3) / 1e9, 1),
@@ -833,8 +853,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--batch", type=int, default=1, help="config 4: tokens per decode step (1 or 8)")
-    ap.add_argument("--tp-allreduce", choices=["p2p", "nccl"], default="p2p",
-                    help="config 3: the o/down all-reduce, over peer memory (default) or NCCL")
+    ap.add_argument("--tp-allreduce", choices=["fused", "p2p", "nccl"], default="fused",
+                    help="config 3: the o/down all-reduce: inside the row-split GEMV over peer memory (default), "
+                         "a separate one-shot peer-memory kernel, or NCCL")
     ap.add_argument("--resident-layers", type=int, default=8,
                     help="config 4: distinct MoE layers held on the GPU and cycled over the 60 (3.4 GB each; "
                          "8 by default, fewer only for profiler captures)")

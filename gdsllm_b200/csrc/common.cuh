@@ -192,6 +192,40 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 
 __device__ __forceinline__ void record_device_error(int bit) { atomicOr(&g_device_error, bit); }
 
+// System-scope flag operations and uncached loads for exchanges with other
+// GPUs over peer memory.
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// 64-bit accesses are single-copy atomic: a (value, epoch) pair stored
+// with one is seen whole or not at all.
+__device__ __forceinline__ void st_volatile_u64(void* p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const void* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_volatile_f32(const float* p) {
+  float v;
+  asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Shared-memory loads on 32-bit shared-window addresses (always LDS, never a
 // generic load).  volatile keeps them ordered after the mbarrier waits.
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {

@@ -713,8 +713,19 @@ int fast_min_smem(int nb, int K, int group) {
   return gemv_smem_layout<F>(batch_tile(nb), K, group, cs, 1, 1).total;
 }
 
+// Tensor-parallel exchange of gdsq_fused_gemv_allreduce (host arrays of the
+// ranks' exchange buffers and flags).
+struct TpExchange {
+  int world;
+  int rank;
+  int rows;
+  const void* const* bufs;
+  void* const* flags;
+};
+
 int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases, const void* x,
-                  void* y, int out_dim, int in_dim, int group, int batch, void* stream_v) {
+                  void* y, int out_dim, int in_dim, int group, int batch, void* stream_v,
+                  const TpExchange* tp = nullptr) {
   t_last_error.clear();
   const char* name = fmt == kFmtQ4_0 ? "q4_0" : fmt == kFmtQ8_0 ? "q8_0" : "affine_q4";
   if (out_dim < 0 || in_dim < 0)
@@ -771,6 +782,21 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
                                  : (long long)in_dim / 2;
 
   const bool shape_ok = in_dim % kChunkCols == 0 && aligned(w, 16) && aligned(x, 16);
+  if (tp != nullptr) {
+    // The exchange lives in the CUDA-core kernel's epilogue (batch 1).
+    if (!shape_ok || batch != 1 || fmt == kFmtAffineQ4)
+      return fail(GDSQ_ERR_UNSUPPORTED, "gemv allreduce: needs Q4_0/Q8_0, batch 1, in_dim %% 256 == 0 and 16-byte "
+                  "aligned weight and input");
+    p.tp_world = tp->world;
+    p.tp_rank = tp->rank;
+    p.tp_rows = tp->rows;
+    for (int r = 0; r < tp->world; ++r) {
+      p.tp_bufs[r] = static_cast<unsigned long long*>(const_cast<void*>(tp->bufs[r]));
+      p.tp_flags[r] = static_cast<int*>(tp->flags[r]);
+    }
+    if (fmt == kFmtQ4_0) return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream);
+    return launch_fast_batch<kFmtQ8_0, 0>(p, *dev, stream);
+  }
   const int tcb = tcb_mode();
   const bool use_tcb = shape_ok && (tcb == 1 || (tcb == -1 && batch >= 5));
   if (use_tcb) {
@@ -1213,6 +1239,29 @@ int gdsq_fused_affine_q4_gemv(const void* weight, const void* scales, const void
                        batch, stream);
 }
 
+int gdsq_fused_gemv_allreduce(int gguf_type, const void* weight, const void* x, void* y, int out_dim, int in_dim,
+                              const void* const* bufs, void* const* flags, int rows_cap, int rank, int world,
+                              void* stream) {
+  t_last_error.clear();
+  if (gguf_type != GDSQ_TYPE_Q4_0 && gguf_type != GDSQ_TYPE_Q8_0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "gemv allreduce: gguf_type %d is neither Q4_0 nor Q8_0", gguf_type);
+  if (world < 1 || world > kTpMaxRanks || rank < 0 || rank >= world)
+    return fail(GDSQ_ERR_INVALID_VALUE, "gemv allreduce: rank %d of world %d (at most %d ranks)", rank, world,
+                kTpMaxRanks);
+  const int rgs = (out_dim + 31) / 32;
+  if (out_dim < 0 || rgs > kTpMaxRowGroups || rgs * 32 > rows_cap)
+    return fail(GDSQ_ERR_INVALID_VALUE, "gemv allreduce: out_dim %d needs %d rows of exchange buffer (have %d, at "
+                "most %d)", out_dim, rgs * 32, rows_cap, kTpMaxRowGroups * 32);
+  if (!bufs || !flags) return fail(GDSQ_ERR_INVALID_VALUE, "gemv allreduce: null buffer arrays");
+  for (int r = 0; r < world; ++r)
+    if (!bufs[r] || !flags[r] || !aligned(bufs[r], 8) || !aligned(flags[r], 4))
+      return fail(GDSQ_ERR_MISALIGNED, "gemv allreduce: rank %d exchange buffer or flags null or misaligned", r);
+  const int fmt = gguf_type == GDSQ_TYPE_Q4_0 ? kFmtQ4_0 : kFmtQ8_0;
+  if (world == 1) return gemv_dispatch(fmt, weight, nullptr, nullptr, x, y, out_dim, in_dim, 0, 1, stream);
+  TpExchange tp{world, rank, rows_cap, bufs, flags};
+  return gemv_dispatch(fmt, weight, nullptr, nullptr, x, y, out_dim, in_dim, 0, 1, stream, &tp);
+}
+
 int gdsq_fused_gemv_group(int gguf_type, int count, const void* const* weights, const int* out_dims,
                           void* const* ys, const void* x, int in_dim, int batch, void* stream_v) {
   t_last_error.clear();
@@ -1376,7 +1425,7 @@ int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* 
   a.in = static_cast<const __half*>(in);
   a.out = static_cast<__half*>(out);
   for (int r = 0; r < world; ++r) {
-    if (!bufs[r] || !flags[r] || !aligned(bufs[r], 16) || !aligned(flags[r], 4))
+    if (!bufs[r] || !flags[r] || !aligned(bufs[r], 8) || !aligned(flags[r], 4))
       return fail(GDSQ_ERR_MISALIGNED, "allreduce: rank %d buffer must be 16-byte aligned and non-null", r);
     a.bufs[r] = static_cast<__half*>(const_cast<void*>(bufs[r]));
     a.flags[r] = static_cast<int*>(flags[r]);

@@ -106,9 +106,122 @@ struct GemvParams {
   int rg_start[5];
   __half* ys[4];
   int ns[4];
+  // Tensor-parallel row split (batch 1, count 1): tp_world > 1 sums each
+  // output row over the ranks inside the kernel (tp_publish /
+  // tp_finish_cta).  tp_bufs[r] = rank r's exchange buffer [2][world]
+  // [tp_rows] of (fp32 value, epoch) words, tp_flags[r] = its flags
+  // [kTpFlagInts]; both mapped into every rank.
+  int tp_world;
+  int tp_rank;
+  int tp_rows;
+  unsigned long long* tp_bufs[8];
+  int* tp_flags[8];
 };
 
 constexpr int kMaxGroup = 4;
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpMaxRowGroups = 1024;
+
+// Tensor-parallel exchange of the row-split GEMV (batch 1, one matrix).
+// Per rank: a buffer [2 slots][world][tp_rows] of 64-bit words, each the
+// fp32 bits of one partial output row (low half) and the call epoch (high
+// half), and an int array [kTpFlagInts] (local only: [kTpEpoch] = the last
+// call finished, [kTpFinCount] = finishers done in the current call); both
+// mapped into every rank.  Call epoch E = [kTpEpoch] + 1, slot E & 1.
+//   tp_publish (the CTA that computed a row group, warp 0): one 64-bit store
+//     of (row value, E) into row `rank` of slot E & 1 of every rank's buffer
+//     (remote ones over NVLink).  The value travels with its epoch in one
+//     single-copy-atomic word, so no fence or flag is needed, and publishing
+//     never waits.
+//   tp_finish_cta (the leaders of the first nf clusters, after their own row
+//     groups): poll (bounded) this rank's own buffer until each row of the
+//     finisher's share carries E for every rank, add the world values in
+//     rank order (fp32, identical bits on every rank) and store fp16.  The
+//     last finisher to count itself done records E in [kTpEpoch].
+// Every finisher reads E before it counts itself, and every publisher reads
+// E before its rows appear, which some finisher waits for; so [kTpEpoch]
+// changes only after every CTA of the call has read it.  The next call's
+// CTAs read it only after this grid completed (programmatic dependent launch
+// waits).  All CTAs but the finishers leave right after publishing.  Two
+// slots suffice: rank A writes slot E & 1 of rank B again in call E + 2,
+// which starts after A's call E + 1 saw B's rows of E + 1, which B writes
+// only after its call E (the last reader of the slot) completed.
+constexpr int kTpFlagInts = 64;
+constexpr int kTpEpoch = 1;
+constexpr int kTpFinCount = 2;
+constexpr int kTpFinishers = 8;
+
+__device__ __forceinline__ int tp_call_epoch(const GemvParams& p) {
+  return *reinterpret_cast<volatile int*>(p.tp_flags[p.tp_rank] + kTpEpoch) + 1;
+}
+
+__device__ __forceinline__ size_t tp_word(const GemvParams& p, int e, int src, int row) {
+  return ((size_t)(e & 1) * p.tp_world + src) * p.tp_rows + row;
+}
+
+__device__ __forceinline__ void tp_publish(const GemvParams& p, int e, int rg, int lane, float v) {
+  const unsigned long long w = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(v);
+  const size_t i = tp_word(p, e, p.tp_rank, rg * 32 + lane);
+  for (int r = 0; r < p.tp_world; ++r) st_volatile_u64(p.tp_bufs[r] + i, w);
+}
+
+// Every thread of finisher f of nf.  Returns false if a wait expired.
+__device__ __noinline__ bool tp_finish_cta(const GemvParams& p, int e, int f, int nf) {
+  __shared__ int s_fail;
+  constexpr int kRows = 8;  // rows per thread per pass
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  const unsigned long long* buf = p.tp_bufs[p.tp_rank];
+  const int rows = p.num_rg * 32;
+  const int per = (rows + nf - 1) / nf;
+  const int lo = f * per;
+  const int hi = min(rows, lo + per);
+  bool ok = true;
+  for (int base = lo + threadIdx.x; base < hi; base += blockDim.x * kRows) {
+    float sum[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) sum[j] = 0.f;
+    for (int q = 0; q < p.tp_world; ++q) {
+      unsigned long long w[kRows];
+      const size_t i0 = tp_word(p, e, q, 0);
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) {
+        const int row = base + j * blockDim.x;
+        w[j] = row < hi ? ld_volatile_u64(buf + i0 + row) : ((unsigned long long)(unsigned)e << 32);
+      }
+      unsigned long long t0 = 0;
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) {
+        const int row = base + j * blockDim.x;
+        while (ok && (int)(w[j] >> 32) != e) {
+          if (t0 == 0) t0 = global_timer_ns();
+          else if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kDevErrBarrierTimeout);
+            ok = false;
+            break;
+          }
+          w[j] = ld_volatile_u64(buf + i0 + row);
+        }
+        sum[j] += __uint_as_float((unsigned)w[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      const int row = base + j * blockDim.x;
+      if (ok && row < hi && row < p.N) p.y[row] = __float2half_rn(sum[j]);
+    }
+  }
+  if (!ok) s_fail = 1;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* own = p.tp_flags[p.tp_rank];
+    if (atomicAdd(own + kTpFinCount, 1) == nf - 1) {
+      own[kTpFinCount] = 0;
+      *reinterpret_cast<volatile int*>(own + kTpEpoch) = e;
+    }
+  }
+  return s_fail == 0;
+}
 
 // Shared-memory carve-up of the fast kernel, identical on host and device.
 struct GemvSmemLayout {
@@ -569,6 +682,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   if (nitems > 0) load_sb(cluster * 32);
 
   pdl_wait_primary();  // activations are produced by the previous kernel
+  // Tensor-parallel exchange: the call's epoch (read after the previous
+  // call's grid completed) and the finisher count (each has a row group).
+  const int tp_e = p.tp_world > 1 && crank == 0 ? tp_call_epoch(p) : 0;
+  const int tp_nf = min(min(nclusters, p.num_rg), kTpFinishers);
   const int ld = L.kslice;  // staged row stride, in elements
   if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
@@ -653,7 +770,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 #pragma unroll
       for (int wv = 0; wv < kGemvWarps; ++wv) v += rd[(wv * B + b) * 32 + l];
       if (cs == 1) {
-        if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
+        if (p.tp_world > 1) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
+        else if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
       } else if (crank != 0) {
         if (item >= 2 && ok && !mbar_wait_cluster(&red_empty[item & 1], par ^ 1)) {
           ok = false;
@@ -667,7 +785,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
           record_device_error(kDevErrBarrierTimeout);
         }
         for (int r = 1; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
-        if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
+        if (p.tp_world > 1) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
+        else if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
         if (item + 2 < nitems) {
           for (int r = 1; r < cs; ++r) mbar_arrive_cluster(map_to_rank(&red_empty[item & 1], r));
         }
@@ -676,6 +795,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
 
   if (cs > 1 && nitems == 0) cluster_wait();  // pairs the early arrive
+  if (p.tp_world > 1 && crank == 0 && cluster < tp_nf) {
+    // The cross-rank sums (one matrix, batch 1), by the first few leaders.
+    if (!tp_finish_cta(p, tp_e, cluster, tp_nf)) ok = false;
+  }
   if (!ok) {
     // A copy never completed.  Record it and wait (bounded) for the copies
     // still in flight into this warp's ring (at most S, starting with the one

@@ -89,18 +89,27 @@ class ColumnParallelGemv:
 
 
 class RowParallelGemv:
-    """y [B, N] = sum over ranks of W[:, cols of rank] . x_local, all-reduced."""
+    """y [B, N] = sum over ranks of W[:, cols of rank] . x_local.
+
+    ``exchange``: None -> NCCL all-reduce after the GEMV; a
+    ``p2p.PeerRowGemv`` -> the sum happens inside the GEMV's epilogue over
+    NVLink peer memory (batch 1, GGUF formats)."""
 
     def __init__(self, weight, n: int, k: int, fmt: str = "q4_0", rank: int = 0, world: int = 1,
-                 group: Optional[dist.ProcessGroup] = None, gemv: Optional[Callable] = None):
+                 group: Optional[dist.ProcessGroup] = None, gemv: Optional[Callable] = None, exchange=None):
         self.n = n
         self.k_local = k // world
         self.weight = weight
+        self.fmt = fmt
         self.world = world
         self.group = group
         self.gemv = gemv or default_gemv(fmt)
+        self.exchange = exchange
 
     def __call__(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.world > 1 and self.exchange is not None and x_local.numel() == self.k_local:
+            w = self.weight[0] if isinstance(self.weight, (tuple, list)) else self.weight
+            return self.exchange(self.fmt, w, x_local, self.n, self.k_local, out)
         y = self.gemv(self.weight, x_local, self.n, self.k_local, out)
         if self.world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)

@@ -205,6 +205,20 @@ GDSQ_API int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gat
 GDSQ_API int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* bufs, void* const* flags,
                                     int cap, int rank, int world, void* stream);
 
+/* A row-split (K-sharded) Q4_0 / Q8_0 GEMV whose output rows are summed over
+ * the tensor-parallel ranks inside the kernel: y = sum over ranks r of
+ * W_r . x_r, fp32 sums added in rank order (identical on every rank), fp16
+ * out.  Batch 1.  bufs / flags: host arrays of `world` device pointers, entry
+ * r = rank r's exchange buffer (2 * world * rows_cap 64-bit words, 8-byte
+ * aligned, zero-initialised: every rank stores its partial rows, each with
+ * the call's epoch, into every rank's buffer) and flags (64 int32,
+ * zero-initialised), mapped into this process (CUDA IPC).  rows_cap >=
+ * out_dim rounded up to 32, out_dim <= 32768.  Every rank must make the same
+ * sequence of calls with the same shapes.  No reference counterpart. */
+GDSQ_API int gdsq_fused_gemv_allreduce(int gguf_type, const void* weight, const void* x, void* y, int out_dim,
+                                       int in_dim, const void* const* bufs, void* const* flags, int rows_cap, int rank,
+                                       int world, void* stream);
+
 /* The routing tail of moe_route (qwen_moe.py:407-413) on router logits fp16
  * [num_tokens][num_experts] (the output of F.linear(x, W_router)): expert_ids
  * int32 [num_tokens][top_k] of the top_k largest logits, largest first (equal

@@ -104,6 +104,58 @@ def _worker(rank, world, port, q):
         res["p2p_err"] = capi.device_error(rank, clear=True)
         torch.cuda.synchronize()
         ar.close()
+        # ---- row split with the all-reduce inside the GEMV epilogue ----
+        from gdsllm_b200.p2p import PeerRowGemv
+        fused = PeerRowGemv(k)
+        worst_f, agree = 0.0, True
+        cases = [("q4_0", synth.q4_0_weight, capi.gemv_q4_0, k, n), ("q8_0", synth.q8_0_weight, capi.gemv_q8_0, k, n),
+                 ("q4_0", synth.q4_0_weight, capi.gemv_q4_0, 4096, 14336),
+                 ("q4_0", synth.q4_0_weight, capi.gemv_q4_0, 1000, 2048)]
+        for ci, (fmt, make, full_gemv, nn, kk) in enumerate(cases):
+            wf = make(nn, kk, seed=20 + ci).to(dev)
+            kl = kk // world
+            wl = tp.split_k_gguf(wf, kk, fmt, rank, world)
+            layer = tp.RowParallelGemv((wl,), nn, kk, fmt, rank, world, exchange=fused)
+            layer_nccl = tp.RowParallelGemv((wl,), nn, kk, fmt, rank, world)
+            for rep in range(3):  # epochs advance per row group
+                xf = synth.activations(1, kk, seed=30 + 7 * ci + rep).to(dev)
+                xl = xf[:, rank * kl:(rank + 1) * kl].contiguous()
+                y_f = layer(xl)
+                y_n = layer_nccl(xl)
+                y_1 = full_gemv(wf, xf, nn, kk)
+                scale = y_1.float().abs().max().item()
+                worst_f = max(worst_f, (y_f.float() - y_1.float()).abs().max().item() / (scale + 1),
+                              (y_f.float() - y_n.float()).abs().max().item() / (scale + 1))
+                both = [torch.empty_like(y_f) for _ in range(world)]
+                dist.all_gather(both, y_f)
+                agree = agree and all(torch.equal(both[0], b) for b in both)
+        # captured in a CUDA graph and replayed with new activations
+        wf = synth.q4_0_weight(k, n, seed=40).to(dev)
+        wl = tp.split_k_gguf(wf, n, "q4_0", rank, world)
+        kl = n // world
+        gx = torch.empty(1, kl, dtype=torch.float16, device=dev)
+        gy = torch.empty(1, k, dtype=torch.float16, device=dev)
+        s0 = torch.cuda.Stream()
+        s0.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s0):
+            fused("q4_0", wl, gx.zero_(), k, kl, out=gy)
+        torch.cuda.current_stream().wait_stream(s0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fused("q4_0", wl, gx, k, kl, out=gy)
+        for it in range(4):
+            xf = synth.activations(1, n, seed=60 + it).to(dev)
+            gx.copy_(xf[:, rank * kl:(rank + 1) * kl])
+            g.replay()
+            y_1 = capi.gemv_q4_0(wf, xf, k, n)
+            torch.cuda.synchronize()
+            worst_f = max(worst_f, (gy.float() - y_1.float()).abs().max().item() / (y_1.float().abs().max().item() + 1))
+        del g
+        res["fused"] = worst_f
+        res["fused_agree"] = agree
+        res["fused_err"] = capi.device_error(rank, clear=True)
+        torch.cuda.synchronize()
+        fused.close()
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -133,3 +185,8 @@ def test_expert_and_tensor_parallel_on_two_gpus():
         # peer all-reduce: fp32 sum vs NCCL's fp16 sum, relative to the value
         assert res["p2p"] <= 2e-3, (rank, res)
         assert res["p2p_err"] == 0, (rank, res)
+        # fused row split: fp32 partials summed in rank order then one fp16
+        # rounding, against the full single-GPU GEMV and the NCCL path
+        assert res["fused"] <= 4e-3, (rank, res)
+        assert res["fused_agree"], (rank, res)   # every rank holds the same bits
+        assert res["fused_err"] == 0, (rank, res)

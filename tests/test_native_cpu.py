@@ -130,6 +130,12 @@ def _moe_gate_up(l, top_k=4, group=128, first=0, count=8, total=8, shared=None):
                                         _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 0, 2, None), b"multiple of 8"),
     (lambda l: l.gdsq_allreduce_sum_f16(FAKE, FAKE, 16384, _arr(ctypes_vp(), [FAKE, FAKE]),
                                         _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 1, 2, None), b"capacity"),
+    (lambda l: l.gdsq_fused_gemv_allreduce(2, FAKE, FAKE, FAKE, 4096, 4096, _arr(ctypes_vp(), [FAKE, FAKE]),
+                                           _arr(ctypes_vp(), [FAKE, FAKE]), 4096, 0, 2, None), b"gguf_type"),
+    (lambda l: l.gdsq_fused_gemv_allreduce(0, FAKE, FAKE, FAKE, 4096, 4096, _arr(ctypes_vp(), [FAKE] * 9),
+                                           _arr(ctypes_vp(), [FAKE] * 9), 4096, 0, 9, None), b"world 9"),
+    (lambda l: l.gdsq_fused_gemv_allreduce(0, FAKE, FAKE, FAKE, 4100, 4096, _arr(ctypes_vp(), [FAKE, FAKE]),
+                                           _arr(ctypes_vp(), [FAKE, FAKE]), 4096, 1, 2, None), b"exchange buffer"),
 ])
 def test_invalid_arguments_of_the_additive_entry_points(call, fragment):
     """The grouped GEMV, MoE and all-reduce entry points reject bad arguments
