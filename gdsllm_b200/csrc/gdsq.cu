@@ -268,10 +268,10 @@ bool plan_override(int* cs, int* stages, int* copy) {
 // divided by an issue-efficiency factor that grows with resident warps (16
 // warps per SM are taken as enough to hide latency).  Candidates whose
 // shared memory does not fit are skipped.
-template <int F, int B, int GS>
+template <int F, int B, int GS, bool TP = false>
 int make_plan_model(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
   using T = GemvFormat<F>;
-  auto kernel = gemv_fast_kernel<F, B, GS>;
+  auto kernel = gemv_fast_kernel<F, B, GS, TP>;
   const int R = (N + 31) / 32;
   const int C = K / kChunkCols;
   int force_cs = 0, force_st = 0, force_cp = 0;
@@ -341,10 +341,10 @@ int make_plan_model(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
 // cs <= 4 with R * cs >= 4 * SMs, then fewer stages or a wider split if
 // shared memory does not fit.  Batches > 1 keep the cost model above (their
 // staged activations make shared memory, hence occupancy, the constraint).
-template <int F, int B, int GS>
+template <int F, int B, int GS, bool TP = false>
 int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
-  if (B > 1) return make_plan_model<F, B, GS>(N, K, dev, out);
-  auto kernel = gemv_fast_kernel<F, B, GS>;
+  if (B > 1) return make_plan_model<F, B, GS, TP>(N, K, dev, out);
+  auto kernel = gemv_fast_kernel<F, B, GS, TP>;
   const int R = (N + 31) / 32;
   const int C = K / kChunkCols;
   int force_cs = 0, force_st = 0, force_cp = 0;
@@ -384,7 +384,7 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
 
 // `wlist` (host array of `p.count` weight pointers) for a grouped launch whose
 // rg_start / ys / ns the caller has filled; nullptr for a plain launch.
-template <int F, int B, int GS>
+template <int F, int B, int GS, bool TP = false>
 int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream, const void* const* wlist = nullptr) {
   if (wlist == nullptr) {
     p.count = 1;
@@ -396,7 +396,7 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream, const 
     for (int m = p.count + 1; m <= kMaxGroup; ++m) p.rg_start[m] = p.rg_start[p.count];
     p.N = p.rg_start[p.count] * 32;  // the planner sees the concatenated rows
   }
-  const uint64_t key = ((uint64_t)F << 60) | ((uint64_t)B << 54) | ((uint64_t)GS << 44) |
+  const uint64_t key = ((uint64_t)TP << 63) | ((uint64_t)F << 60) | ((uint64_t)B << 54) | ((uint64_t)GS << 44) |
                        ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
   GemvPlan plan;
   int ocs, ost, ocp;
@@ -411,7 +411,7 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream, const 
     }
   }
   if (!have) {
-    int st = make_plan<F, B, GS>(p.N, p.K, dev, &plan);
+    int st = make_plan<F, B, GS, TP>(p.N, p.K, dev, &plan);
     if (st != GDSQ_OK) return st;
     if (!forced) {
       std::lock_guard<std::mutex> lock(g_plan_mutex);
@@ -425,7 +425,7 @@ int launch_fast(GemvParams p, const DeviceInfo& dev, cudaStream_t stream, const 
     if (mst != GDSQ_OK) return mst;
   }
   for (int m = p.count; m < kMaxGroup; ++m) maps[m] = maps[0];
-  auto kernel = gemv_fast_kernel<F, B, GS>;
+  auto kernel = gemv_fast_kernel<F, B, GS, TP>;
   cudaError_t e = ensure_smem(kernel, plan.smem, dev.ordinal);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
   p.cs = plan.cs;
@@ -794,8 +794,10 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
       p.tp_bufs[r] = static_cast<unsigned long long*>(const_cast<void*>(tp->bufs[r]));
       p.tp_flags[r] = static_cast<int*>(tp->flags[r]);
     }
-    if (fmt == kFmtQ4_0) return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream);
-    return launch_fast_batch<kFmtQ8_0, 0>(p, *dev, stream);
+    p.tp_own_buf = p.tp_bufs[tp->rank];
+    p.tp_own_flags = p.tp_flags[tp->rank];
+    if (fmt == kFmtQ4_0) return launch_fast<kFmtQ4_0, 1, 0, true>(p, *dev, stream);
+    return launch_fast<kFmtQ8_0, 1, 0, true>(p, *dev, stream);
   }
   const int tcb = tcb_mode();
   const bool use_tcb = shape_ok && (tcb == 1 || (tcb == -1 && batch >= 5));

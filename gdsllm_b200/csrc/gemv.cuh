@@ -106,8 +106,8 @@ struct GemvParams {
   int rg_start[5];
   __half* ys[4];
   int ns[4];
-  // Tensor-parallel row split (batch 1, count 1): tp_world > 1 sums each
-  // output row over the ranks inside the kernel (tp_publish /
+  // Tensor-parallel row split (the TP instantiation; batch 1, count 1,
+  // tp_world > 1): each output row is summed over the ranks inside the kernel (tp_publish /
   // tp_finish_cta).  tp_bufs[r] = rank r's exchange buffer [2][world]
   // [tp_rows] of (fp32 value, epoch) words, tp_flags[r] = its flags
   // [kTpFlagInts]; both mapped into every rank.
@@ -116,6 +116,8 @@ struct GemvParams {
   int tp_rows;
   unsigned long long* tp_bufs[8];
   int* tp_flags[8];
+  unsigned long long* tp_own_buf;  // tp_bufs[tp_rank]
+  int* tp_own_flags;               // tp_flags[tp_rank]
 };
 
 constexpr int kMaxGroup = 4;
@@ -151,28 +153,32 @@ constexpr int kTpEpoch = 1;
 constexpr int kTpFinCount = 2;
 constexpr int kTpFinishers = 8;
 
-__device__ __forceinline__ int tp_call_epoch(const GemvParams& p) {
-  return *reinterpret_cast<volatile int*>(p.tp_flags[p.tp_rank] + kTpEpoch) + 1;
+__device__ __forceinline__ int tp_call_epoch(const int* own_flags) {
+  return *reinterpret_cast<const volatile int*>(own_flags + kTpEpoch) + 1;
 }
 
-__device__ __forceinline__ size_t tp_word(const GemvParams& p, int e, int src, int row) {
-  return ((size_t)(e & 1) * p.tp_world + src) * p.tp_rows + row;
+__device__ __forceinline__ size_t tp_word(int e, int world, int rows_cap, int src, int row) {
+  return ((size_t)(e & 1) * world + src) * rows_cap + row;
 }
 
 __device__ __forceinline__ void tp_publish(const GemvParams& p, int e, int rg, int lane, float v) {
   const unsigned long long w = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(v);
-  const size_t i = tp_word(p, e, p.tp_rank, rg * 32 + lane);
-  for (int r = 0; r < p.tp_world; ++r) st_volatile_u64(p.tp_bufs[r] + i, w);
+  const size_t i = tp_word(e, p.tp_world, p.tp_rows, p.tp_rank, rg * 32 + lane);
+#pragma unroll
+  for (int r = 0; r < kTpMaxRanks; ++r)  // constant indices keep the parameter array in place
+    if (r < p.tp_world) st_volatile_u64(p.tp_bufs[r] + i, w);
 }
 
-// Every thread of finisher f of nf.  Returns false if a wait expired.
-__device__ __noinline__ bool tp_finish_cta(const GemvParams& p, int e, int f, int nf) {
+// Every thread of finisher f of nf.  Scalar arguments only, so the kernel's
+// parameter block is never copied to local memory for the call.  Returns
+// false if a wait expired.
+__device__ __noinline__ bool tp_finish_cta(const unsigned long long* buf, int* own, __half* y, int N, int num_rg,
+                                           int world, int rows_cap, int e, int f, int nf) {
   __shared__ int s_fail;
   constexpr int kRows = 8;  // rows per thread per pass
   if (threadIdx.x == 0) s_fail = 0;
   __syncthreads();
-  const unsigned long long* buf = p.tp_bufs[p.tp_rank];
-  const int rows = p.num_rg * 32;
+  const int rows = num_rg * 32;
   const int per = (rows + nf - 1) / nf;
   const int lo = f * per;
   const int hi = min(rows, lo + per);
@@ -181,9 +187,9 @@ __device__ __noinline__ bool tp_finish_cta(const GemvParams& p, int e, int f, in
     float sum[kRows];
 #pragma unroll
     for (int j = 0; j < kRows; ++j) sum[j] = 0.f;
-    for (int q = 0; q < p.tp_world; ++q) {
+    for (int q = 0; q < world; ++q) {
       unsigned long long w[kRows];
-      const size_t i0 = tp_word(p, e, q, 0);
+      const size_t i0 = tp_word(e, world, rows_cap, q, 0);
 #pragma unroll
       for (int j = 0; j < kRows; ++j) {
         const int row = base + j * blockDim.x;
@@ -208,13 +214,12 @@ __device__ __noinline__ bool tp_finish_cta(const GemvParams& p, int e, int f, in
 #pragma unroll
     for (int j = 0; j < kRows; ++j) {
       const int row = base + j * blockDim.x;
-      if (ok && row < hi && row < p.N) p.y[row] = __float2half_rn(sum[j]);
+      if (ok && row < hi && row < N) y[row] = __float2half_rn(sum[j]);
     }
   }
   if (!ok) s_fail = 1;
   __syncthreads();
   if (threadIdx.x == 0) {
-    int* own = p.tp_flags[p.tp_rank];
     if (atomicAdd(own + kTpFinCount, 1) == nf - 1) {
       own[kTpFinCount] = 0;
       *reinterpret_cast<volatile int*>(own + kTpEpoch) = e;
@@ -562,7 +567,11 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
 
 // ---------------------------------------------------------------------------
 
-template <int F, int B, int GS>
+// TP: the tensor-parallel row split (batch 1, one matrix, tp_world > 1):
+// the epilogue publishes the rows to the ranks and the first few leader CTAs
+// finish the cross-rank sums (tp_publish / tp_finish_cta).  A separate
+// instantiation, so the plain kernels carry none of its code or registers.
+template <int F, int B, int GS, bool TP = false>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_fast_kernel(const GemvParams p, const __grid_constant__ CUtensorMap wmap,
                      const __grid_constant__ CUtensorMap wmap1, const __grid_constant__ CUtensorMap wmap2,
@@ -684,8 +693,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   pdl_wait_primary();  // activations are produced by the previous kernel
   // Tensor-parallel exchange: the call's epoch (read after the previous
   // call's grid completed) and the finisher count (each has a row group).
-  const int tp_e = p.tp_world > 1 && crank == 0 ? tp_call_epoch(p) : 0;
-  const int tp_nf = min(min(nclusters, p.num_rg), kTpFinishers);
+  const int tp_e = TP && crank == 0 ? tp_call_epoch(p.tp_own_flags) : 0;
   const int ld = L.kslice;  // staged row stride, in elements
   if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
@@ -770,7 +778,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 #pragma unroll
       for (int wv = 0; wv < kGemvWarps; ++wv) v += rd[(wv * B + b) * 32 + l];
       if (cs == 1) {
-        if (p.tp_world > 1) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
+        if constexpr (TP) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
         else if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
       } else if (crank != 0) {
         if (item >= 2 && ok && !mbar_wait_cluster(&red_empty[item & 1], par ^ 1)) {
@@ -785,7 +793,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
           record_device_error(kDevErrBarrierTimeout);
         }
         for (int r = 1; r < cs; ++r) v += sl[(r * B + b) * 32 + l];
-        if (p.tp_world > 1) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
+        if constexpr (TP) tp_publish(p, tp_e, cluster + item * nclusters, l, v);  // batch 1: warp 0
         else if (b < p.nb && l < nvalid) ym[(size_t)b * Nm + row0 + l] = __float2half_rn(v);
         if (item + 2 < nitems) {
           for (int r = 1; r < cs; ++r) mbar_arrive_cluster(map_to_rank(&red_empty[item & 1], r));
@@ -795,9 +803,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
 
   if (cs > 1 && nitems == 0) cluster_wait();  // pairs the early arrive
-  if (p.tp_world > 1 && crank == 0 && cluster < tp_nf) {
+  if constexpr (TP) {
     // The cross-rank sums (one matrix, batch 1), by the first few leaders.
-    if (!tp_finish_cta(p, tp_e, cluster, tp_nf)) ok = false;
+    const int tp_nf = min(min(nclusters, p.num_rg), kTpFinishers);
+    if (crank == 0 && cluster < tp_nf &&
+        !tp_finish_cta(p.tp_own_buf, p.tp_own_flags, p.y, p.N, p.num_rg, p.tp_world, p.tp_rows, tp_e, cluster,
+                       tp_nf))
+      ok = false;
   }
   if (!ok) {
     // A copy never completed.  Record it and wait (bounded) for the copies
