@@ -781,8 +781,8 @@ def bench_config4(args, dist):
     """Qwen-MoE-shaped affine-Q4 MoE decode, expert-parallel over the ranks
     60 MoE layers (8 distinct resident layers cycled),
     512 experts + 1 shared (hidden 4096, intermediate 1024), fp16 router with
-    top-10; experts split 512 / N per GPU, one NCCL all-reduce of the fp32
-    partial sums per layer.  One step = one decode step of `--batch` tokens."""
+    top-10; experts split 512 / N per GPU, one all-reduce of the fp32
+    partial sums per layer (over NVLink peer memory, or NCCL).  One step = one decode step of `--batch` tokens."""
     from gdsllm_b200 import capi, ep, moe
     peak, peak_kind = load_peaks()
     capi.set_pdl(bool(args.pdl))
@@ -803,7 +803,11 @@ def bench_config4(args, dist):
             router=router, gate=st(I, H, base + 1 + rank * 8, count), up=st(I, H, base + 2 + rank * 8, count),
             down=st(H, I, base + 3 + rank * 8, count), group=G, expert_first=first, expert_total=E,
             shared=(st(I, H, base + 4, 1), st(I, H, base + 5, 1), st(H, I, base + 6, 1)), shared_gate=sgate))
-    mods = [ep.ExpertParallelMoE(layer, top_k=TOPK) for layer in layers] if ws > 1 else None
+    exch = None
+    if ws > 1 and args.ep_allreduce == "peer":
+        from gdsllm_b200.p2p import PeerWordAllReduce
+        exch = PeerWordAllReduce(B * H, device=dev)
+    mods = [ep.ExpertParallelMoE(layer, top_k=TOPK, allreduce=exch) for layer in layers] if ws > 1 else None
     x0 = synth.activations(B, H, seed=3, device=dev)
 
     def step(stream):
@@ -828,15 +832,19 @@ def bench_config4(args, dist):
     g = capture(step)
     ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
     del g
+    if exch is not None:
+        exch.close()
     step_s = ms / args.steps / 1e3
     return {"metric": "Qwen-MoE-shaped affine-Q4 MoE decode tok/s, expert-parallel (60 layers x (router top-10 + "
-                      "fused expert gather + shared expert), NCCL all-reduce per layer)",
+                      "fused expert gather + shared expert), all-reduce of the partials per layer)",
             "value": round(B / step_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random affine-Q4 experts, config 4 shapes)",
             "config": {"workload": f"config 4: {E} experts + shared, hidden 4096, expert intermediate 1024, top-10, "
                                    f"batch {B}, 60 layers cycling {NPHYS} resident layers",
                        "parallelism": f"ep{ws}", "experts_per_gpu": count,
+                       "allreduce": ("one-shot (value, epoch) words over NVLink peer memory (gdsq_allreduce_sum_words)"
+                                     if exch is not None else "NCCL") if ws > 1 else None,
                        "touched_weight_gb_per_step": round(touched / 1e9, 3),
                        "l2": f"{NPHYS} resident layers of {E * 3 * 2.23 / 1e3:.1f} GB each (> L2)"},
             "roofline": {"bound": "hbm", "achieved": round(touched / ws / step_s / 1e9, 1), "peak": peak,
@@ -856,6 +864,8 @@ def main():
     ap.add_argument("--tp-allreduce", choices=["fused", "p2p", "nccl"], default="fused",
                     help="config 3: the o/down all-reduce: inside the row-split GEMV over peer memory (default), "
                          "a separate one-shot peer-memory kernel, or NCCL")
+    ap.add_argument("--ep-allreduce", choices=["peer", "nccl"], default="peer",
+                    help="config 4: the per-layer sum of the partials over peer memory (default) or NCCL")
     ap.add_argument("--resident-layers", type=int, default=8,
                     help="config 4: distinct MoE layers held on the GPU and cycled over the 60 (3.4 GB each; "
                          "8 by default, fewer only for profiler captures)")

@@ -1444,6 +1444,46 @@ int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* 
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "allreduce launch");
 }
 
+int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, const void* const* bufs, void* epochs,
+                             int cap, int rank, int world, void* stream_v) {
+  t_last_error.clear();
+  if (elem_type != GDSQ_ELEM_F16 && elem_type != GDSQ_ELEM_F32)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: elem_type %d is neither fp16 nor fp32", elem_type);
+  if (world < 1 || world > kP2PMaxRanks || rank < 0 || rank >= world)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: rank %d of world %d (at most %d ranks)", rank, world,
+                kP2PMaxRanks);
+  if (n < 0 || n > cap || (n + kLLElemsPerCta - 1) / kLLElemsPerCta > kLLMaxCtas)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: n %d must be <= capacity %d and <= %d", n, cap,
+                kLLMaxCtas * kLLElemsPerCta);
+  if (n == 0) return GDSQ_OK;
+  if (!in || !out || !bufs || !epochs) return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: null pointer");
+  const int esz = elem_type == GDSQ_ELEM_F32 ? 4 : 2;
+  if (!aligned(in, esz) || !aligned(out, esz) || !aligned(epochs, 4))
+    return fail(GDSQ_ERR_MISALIGNED, "allreduce words: input, output or epochs misaligned");
+  LLArgs a = {};
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !aligned(bufs[r], 8))
+      return fail(GDSQ_ERR_MISALIGNED, "allreduce words: rank %d buffer must be 8-byte aligned and non-null", r);
+    a.bufs[r] = static_cast<unsigned long long*>(const_cast<void*>(bufs[r]));
+  }
+  a.own = a.bufs[rank];
+  a.in = in;
+  a.out = out;
+  a.epochs = static_cast<int*>(epochs);
+  a.n = n;
+  a.cap = cap;
+  a.rank = rank;
+  a.world = world;
+  const int grid = (n + kLLElemsPerCta - 1) / kLLElemsPerCta;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  cudaError_t e = elem_type == GDSQ_ELEM_F32
+                      ? launch(allreduce_ll_kernel<float>, dim3(grid), dim3(kLLThreads), 0, stream,
+                               g_pdl_enabled != 0, a)
+                      : launch(allreduce_ll_kernel<__half>, dim3(grid), dim3(kLLThreads), 0, stream,
+                               g_pdl_enabled != 0, a);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "allreduce words launch");
+}
+
 int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,
                    const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
                    void* shared_weights, void* stream_v) {

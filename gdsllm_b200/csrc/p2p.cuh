@@ -22,6 +22,8 @@
 // expires sets device error bit 1, skips the remaining waits and returns.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace gdsq {
@@ -103,6 +105,120 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_oneshot_kernel(const P2
   }
   __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(own + a.rank) = e;
+}
+
+// One-shot all-reduce (sum) with (value, epoch) words: the expert-parallel
+// exchange of the fp32 MoE partials ([B, hidden], one per layer), and any
+// fp16 / fp32 vector up to kLLMaxCtas * kLLElemsPerCta elements.
+//
+// Every rank owns a buffer [2 slots][world][cap] of 64-bit words (fp32 bits
+// low, epoch high), mapped into every peer, and a local int epoch per CTA.
+// CTA c handles elements [c * kLLElemsPerCta, (c + 1) * kLLElemsPerCta):
+//   1. epoch e = own epochs[c] + 1 (read after the previous kernel completed);
+//   2. store (value, e) for each element into row `rank` of slot e & 1 of
+//      every rank's buffer -- one single-copy-atomic 64-bit store each, so
+//      no fence or flag is needed;
+//   3. poll (bounded) this rank's own buffer until every rank's word of each
+//      element carries e, add them in rank order in fp32 (identical bits on
+//      every rank), write the output;
+//   4. record e in epochs[c].
+// Two slots suffice: a rank writes slot e & 1 of a peer again in call e + 2,
+// which starts after its call e + 1 saw the peer's words of e + 1, which the
+// peer stores only after its call e (the last reader of the slot) completed.
+// No rank waits on anything another rank must wait for: each rank's stores
+// come before its own waits.
+constexpr int kLLThreads = 256;
+constexpr int kLLPerThread = 4;
+constexpr int kLLElemsPerCta = kLLThreads * kLLPerThread;
+constexpr int kLLMaxCtas = 32;
+
+struct LLArgs {
+  const void* in;
+  void* out;
+  unsigned long long* bufs[kP2PMaxRanks];  // each rank's word buffer
+  const unsigned long long* own;           // bufs[rank]
+  int* epochs;                             // this rank's [kLLMaxCtas] (local only)
+  int n;
+  int cap;
+  int rank;
+  int world;
+};
+
+template <typename T>
+__device__ __forceinline__ float ll_load(const T* p) {
+  if constexpr (std::is_same<T, float>::value) return *p;
+  else return __half2float(*p);
+}
+
+template <typename T>
+__device__ __forceinline__ void ll_store(T* p, float v) {
+  if constexpr (std::is_same<T, float>::value) *p = v;
+  else *p = __float2half_rn(v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const LLArgs a) {
+  __shared__ int s_fail;
+  const int c = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the input is the previous kernel's output; the epoch its predecessor's
+  if (threadIdx.x == 0) s_fail = 0;
+  const int e = *reinterpret_cast<volatile int*>(a.epochs + c) + 1;
+  const int base = c * kLLElemsPerCta + threadIdx.x;
+  const size_t slot = (size_t)(e & 1) * a.world;
+  const unsigned long long tag = (unsigned long long)(unsigned)e << 32;
+  const T* in = static_cast<const T*>(a.in);
+#pragma unroll
+  for (int j = 0; j < kLLPerThread; ++j) {
+    const int i = base + j * kLLThreads;
+    if (i < a.n) {
+      const unsigned long long w = tag | __float_as_uint(ll_load(in + i));
+      const size_t off = (slot + a.rank) * a.cap + i;
+#pragma unroll
+      for (int r = 0; r < kP2PMaxRanks; ++r)
+        if (r < a.world) st_volatile_u64(a.bufs[r] + off, w);
+    }
+  }
+  __syncthreads();
+  float sum[kLLPerThread];
+#pragma unroll
+  for (int j = 0; j < kLLPerThread; ++j) sum[j] = 0.f;
+  bool ok = true;
+  unsigned long long t0 = 0;
+  for (int q = 0; q < a.world; ++q) {
+    const unsigned long long* src = a.own + (slot + q) * a.cap;
+    unsigned long long w[kLLPerThread];
+#pragma unroll
+    for (int j = 0; j < kLLPerThread; ++j) {
+      const int i = base + j * kLLThreads;
+      w[j] = i < a.n ? ld_volatile_u64(src + i) : tag;
+    }
+#pragma unroll
+    for (int j = 0; j < kLLPerThread; ++j) {
+      while (ok && (w[j] >> 32) != (unsigned long long)(unsigned)e) {
+        if (t0 == 0) {
+          t0 = global_timer_ns();
+        } else if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kDevErrBarrierTimeout);
+          ok = false;
+          break;
+        }
+        w[j] = ld_volatile_u64(src + base + j * kLLThreads);
+      }
+      sum[j] += __uint_as_float((unsigned)w[j]);
+    }
+  }
+  if (!ok) s_fail = 1;
+  __syncthreads();
+  if (s_fail == 0) {
+    T* out = static_cast<T*>(a.out);
+#pragma unroll
+    for (int j = 0; j < kLLPerThread; ++j) {
+      const int i = base + j * kLLThreads;
+      if (i < a.n) ll_store(out + i, sum[j]);
+    }
+  }
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(a.epochs + c) = e;
 }
 
 }  // namespace gdsq

@@ -39,11 +39,13 @@ class ExpertParallelMoE:
     ``layer`` holds this rank's experts (``expert_first``/``expert_total`` set
     accordingly).  ``partial`` computes the rank's fp32 partial sum; it is
     ``moe.moe_partial`` (the CUDA kernels) unless a test substitutes a
-    checker.
+    checker.  ``allreduce`` sums the partial in place over the ranks, e.g. a
+    ``p2p.PeerWordAllReduce`` over NVLink peer memory; None uses NCCL.
     """
 
     def __init__(self, layer: moe.MoeLayer, group: Optional[dist.ProcessGroup] = None,
-                 top_k: int = 10, partial: Optional[Callable] = None, router: Optional[Callable] = None):
+                 top_k: int = 10, partial: Optional[Callable] = None, router: Optional[Callable] = None,
+                 allreduce: Optional[Callable] = None):
         self.layer = layer
         self.group = group
         self.top_k = top_k
@@ -55,6 +57,7 @@ class ExpertParallelMoE:
                              f"{layer.expert_first + layer.num_local}), expected [{first}, {first + count})")
         self.partial = partial or moe.moe_partial
         self.router = router or moe.route
+        self.allreduce = allreduce  # in-place sum of the fp32 partial; None -> NCCL
 
     def forward(self, x: torch.Tensor, out32: Optional[torch.Tensor] = None) -> torch.Tensor:
         x2d = x.reshape(-1, x.shape[-1])
@@ -62,7 +65,10 @@ class ExpertParallelMoE:
         ids, weights, sw = self.router(x2d, self.layer.router, self.top_k, sg)
         y32 = self.partial(x2d, ids, weights, self.layer, out=out32, include_shared=self.rank == 0,
                            shared_weights=sw)
-        dist.all_reduce(y32, op=dist.ReduceOp.SUM, group=self.group)
+        if self.allreduce is not None:
+            self.allreduce(y32)
+        else:
+            dist.all_reduce(y32, op=dist.ReduceOp.SUM, group=self.group)
         return moe.finish(y32, x)
 
     __call__ = forward

@@ -91,6 +91,39 @@ class PeerAllReduce:
         self.peer.close()
 
 
+WORDS_MAX_ELEMS = 32768
+WORDS_EPOCHS = 32  # one int per CTA of the word all-reduce
+
+
+class PeerWordAllReduce:
+    """One-shot sum of an fp16 or fp32 vector over the ranks with (value,
+    epoch) 64-bit words (gdsq_allreduce_sum_words): every rank stores its
+    elements into every rank's buffer and waits only on its own."""
+
+    def __init__(self, capacity: int, group: Optional[dist.ProcessGroup] = None, device=None):
+        if capacity > WORDS_MAX_ELEMS:
+            raise ValueError(f"capacity {capacity}: at most {WORDS_MAX_ELEMS} elements")
+        self.cap = capacity
+        world = dist.get_world_size(group)
+        # the flag array doubles as this rank's per-CTA epochs (never read by the peers)
+        self.peer = PeerBuffers(2 * world * self.cap * 8, WORDS_EPOCHS, group, device)
+        self.rank, self.world = self.peer.rank, self.peer.world
+
+    def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Sum of ``t`` (fp16 or fp32, contiguous) over the ranks; in place
+        unless ``out`` is given."""
+        out = t if out is None else out
+        kind = {torch.float16: 0, torch.float32: 1}[t.dtype]
+        stream = torch.cuda.current_stream(t.device).cuda_stream
+        check(lib().gdsq_allreduce_sum_words(kind, t.data_ptr(), out.data_ptr(), t.numel(), self.peer.bufs,
+                                             self.peer.flags_t.data_ptr(), self.cap, self.rank, self.world, stream),
+              "gdsq_allreduce_sum_words")
+        return out
+
+    def close(self):
+        self.peer.close()
+
+
 TP_MAX_ROW_GROUPS = 1024
 TP_FLAG_INTS = 64  # call epoch and finisher count (local only)
 

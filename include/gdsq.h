@@ -205,6 +205,24 @@ GDSQ_API int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gat
 GDSQ_API int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* bufs, void* const* flags,
                                     int cap, int rank, int world, void* stream);
 
+#define GDSQ_ELEM_F16 0
+#define GDSQ_ELEM_F32 1
+
+/* out[i] = sum over ranks r (in rank order, fp32) of in_r[i], fp16 or fp32
+ * (elem_type GDSQ_ELEM_F16 / GDSQ_ELEM_F32), over NVLink peer memory: every
+ * rank stores each element with the call's epoch as one 64-bit word into
+ * every rank's buffer and waits only on its own buffer (no flags).  The
+ * expert-parallel exchange of the MoE partial sums (no reference
+ * counterpart: the reference runs one GPU).  bufs: host array of `world`
+ * device pointers, entry r = rank r's buffer (2 * world * cap 64-bit words,
+ * 8-byte aligned, zero-initialised) mapped into this process (CUDA IPC);
+ * epochs: this rank's own 32 int32 (zero-initialised, not shared).  n <= cap,
+ * n <= 32768.  Every rank must make the same sequence of calls.  A peer that
+ * does not arrive within 1 s sets device error bit 1 and the call leaves its
+ * output unwritten. */
+GDSQ_API int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, const void* const* bufs,
+                                      void* epochs, int cap, int rank, int world, void* stream);
+
 /* A row-split (K-sharded) Q4_0 / Q8_0 GEMV whose output rows are summed over
  * the tensor-parallel ranks inside the kernel: y = sum over ranks r of
  * W_r . x_r, fp32 sums added in rank order (identical on every rank), fp16

@@ -52,6 +52,41 @@ def _worker(rank, world, port, q):
         y_one = moe.moe_mlp_decode(x, full, 10)
         res["ep"] = (y_ep.float() - y_one.float()).abs().max().item()
         res["ep_scale"] = y_one.float().abs().max().item()
+        # the same layer with the partials summed over peer memory (rank-order
+        # fp32 sums; two ranks add a + b exactly as NCCL does)
+        from gdsllm_b200.p2p import PeerWordAllReduce
+        words = PeerWordAllReduce(8 * hidden)
+        y_ep_words = ep.ExpertParallelMoE(local, top_k=10, allreduce=words)(x)
+        res["ep_words_equal"] = torch.equal(y_ep_words, y_ep)
+        worst_w = 0.0
+        for it, (nel, dt) in enumerate([(8 * hidden, torch.float32), (1000, torch.float32), (4096, torch.float16),
+                                        (8 * hidden, torch.float32), (7, torch.float16)]):
+            t = torch.randn(nel, generator=torch.Generator().manual_seed(200 + 10 * it + rank)).to(dt).to(dev)
+            ref = t.clone().float()   # .float() of an fp32 tensor is the tensor itself
+            dist.all_reduce(ref)
+            out = words(t.clone())
+            worst_w = max(worst_w, ((out.float() - ref).abs() / (ref.abs() + 1)).max().item())
+        gin = torch.empty(8 * hidden, dtype=torch.float32, device=dev)
+        s0 = torch.cuda.Stream()
+        s0.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s0):
+            words(gin.zero_())
+        torch.cuda.current_stream().wait_stream(s0)
+        g = torch.cuda.CUDAGraph()
+        gout = torch.empty_like(gin)
+        with torch.cuda.graph(g):
+            words(gin, out=gout)
+        for it in range(4):
+            gin.copy_(torch.randn(8 * hidden, generator=torch.Generator().manual_seed(300 + it + 10 * rank)).to(dev))
+            g.replay()
+            ref = gin.clone()
+            dist.all_reduce(ref)
+            torch.cuda.synchronize()
+            worst_w = max(worst_w, ((gout - ref).abs() / (ref.abs() + 1)).max().item())
+        del g
+        res["words"] = worst_w
+        res["words_err"] = capi.device_error(rank, clear=True)
+        words.close()
         # ---- tensor parallel Q4_0: column split then row split + all-reduce ----
         n, k = 4096, 8192
         w = synth.q4_0_weight(n, k, seed=11).to(dev)
@@ -185,6 +220,9 @@ def test_expert_and_tensor_parallel_on_two_gpus():
         # peer all-reduce: fp32 sum vs NCCL's fp16 sum, relative to the value
         assert res["p2p"] <= 2e-3, (rank, res)
         assert res["p2p_err"] == 0, (rank, res)
+        assert res["ep_words_equal"], (rank, res)
+        assert res["words"] <= 1e-3, (rank, res)   # fp32 rank-order sum vs NCCL (fp16 inputs summed in fp32)
+        assert res["words_err"] == 0, (rank, res)
         # fused row split: fp32 partials summed in rank order then one fp16
         # rounding, against the full single-GPU GEMV and the NCCL path
         assert res["fused"] <= 4e-3, (rank, res)

@@ -130,6 +130,14 @@ def _moe_gate_up(l, top_k=4, group=128, first=0, count=8, total=8, shared=None):
                                         _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 0, 2, None), b"multiple of 8"),
     (lambda l: l.gdsq_allreduce_sum_f16(FAKE, FAKE, 16384, _arr(ctypes_vp(), [FAKE, FAKE]),
                                         _arr(ctypes_vp(), [FAKE, FAKE]), 8192, 1, 2, None), b"capacity"),
+    (lambda l: l.gdsq_allreduce_sum_words(5, FAKE, FAKE, 64, _arr(ctypes_vp(), [FAKE, FAKE]), FAKE, 64, 0, 2,
+                                          None), b"elem_type"),
+    (lambda l: l.gdsq_allreduce_sum_words(1, FAKE, FAKE, 64, _arr(ctypes_vp(), [FAKE] * 9), FAKE, 64, 0, 9,
+                                          None), b"world 9"),
+    (lambda l: l.gdsq_allreduce_sum_words(1, FAKE, FAKE, 65, _arr(ctypes_vp(), [FAKE, FAKE]), FAKE, 64, 0, 2,
+                                          None), b"capacity"),
+    (lambda l: l.gdsq_allreduce_sum_words(1, FAKE, FAKE, 40000, _arr(ctypes_vp(), [FAKE, FAKE]), FAKE, 40000, 0,
+                                          2, None), b"32768"),
     (lambda l: l.gdsq_fused_gemv_allreduce(2, FAKE, FAKE, FAKE, 4096, 4096, _arr(ctypes_vp(), [FAKE, FAKE]),
                                            _arr(ctypes_vp(), [FAKE, FAKE]), 4096, 0, 2, None), b"gguf_type"),
     (lambda l: l.gdsq_fused_gemv_allreduce(0, FAKE, FAKE, FAKE, 4096, 4096, _arr(ctypes_vp(), [FAKE] * 9),
