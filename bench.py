@@ -297,22 +297,35 @@ def capture(fn):
     return g
 
 
-def time_graph(g, steps, warmup, dist, clocks=None):
+STEP_STATS = {}
+
+
+def time_graph(g, steps, warmup, dist, clocks=None, per_step=False):
+    """Replays `g` `steps` times between CUDA events on the current stream;
+    returns (max over ranks of the total ms, clock samples).  With
+    `per_step`, an event between replays also gives this rank's per-step
+    p10 / p50 / p90 (ms) in STEP_STATS."""
     for _ in range(warmup):
         g.replay()
     torch.cuda.synchronize()
     dist.barrier()
     if clocks:
         clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1 if per_step else 2)]
     torch.cuda.synchronize()
-    start.record()
-    for _ in range(steps):
+    evs[0].record()
+    for i in range(steps):
         g.replay()
-    end.record()
+        if per_step:
+            evs[i + 1].record()
+    evs[-1].record()
     torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
+    ms = evs[0].elapsed_time(evs[-1])
     info = clocks.stop() if clocks else None
+    if per_step:
+        per = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
+        pick = lambda q: round(per[min(steps - 1, int(q * steps))], 4)
+        STEP_STATS.update({"p10": pick(0.1), "p50": pick(0.5), "p90": pick(0.9), "unit": "ms", "rank": dist.rank})
     dist.barrier()
     return dist.max(ms), info
 
@@ -429,7 +442,8 @@ def bench_ours(args, dist):
 
     g = capture(fn)
     clocks = dist.clocks
-    ms, clock_info = time_graph(g, args.steps, args.warmup, dist, clocks)
+    ms, clock_info = time_graph(g, args.steps, args.warmup, dist, clocks, per_step=True)
+    step_stats = dict(STEP_STATS)
     tok_s = args.steps * dist.world / (ms / 1e3)
     del g
     g1 = capture(fn_single)
@@ -466,8 +480,8 @@ def bench_ours(args, dist):
         "metric": "LLaMA-7B Q4_0 batch-1 decode tok/s through the fused dequant-GEMV path "
                   "(224 Q4_0 projections + Q8_0 lm_head per token)",
         "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "step_ms": step_stats,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded random Q4_0/Q8_0 weights per BASELINE config 0/1 distributions)",
         "config": {"workload": "config 1: LLaMA-7B-shaped decode token, hot path only, batch 1",
                    "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
