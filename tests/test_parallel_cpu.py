@@ -81,6 +81,18 @@ def _ep_worker(rank, world, port, q):
         layer = ep.ExpertParallelMoE(local, top_k=TOP_K, partial=oracle_partial, router=moe.route_torch)
         x = synth.activations(NTOK, HIDDEN, seed=5)
         y = layer(x)
+        # an injected in-place sum (the peer-memory all-reduce on GPUs) replaces the default
+        calls = []
+
+        def summed(t):
+            calls.append((tuple(t.shape), t.dtype))
+            dist.all_reduce(t)
+            return t
+
+        y2 = ep.ExpertParallelMoE(local, top_k=TOP_K, partial=oracle_partial, router=moe.route_torch,
+                                  allreduce=summed)(x)
+        assert calls == [((NTOK, HIDDEN), torch.float32)], calls
+        assert torch.equal(y, y2)
         q.put((rank, y.numpy()))
     finally:
         dist.destroy_process_group()
