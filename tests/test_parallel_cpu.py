@@ -198,3 +198,49 @@ def test_tensor_parallel_two_ranks_matches_full_product():
     np.testing.assert_allclose(cols, exact, rtol=1e-5, atol=1e-4)
     for rank, y_row, _ in out:
         np.testing.assert_allclose(y_row, exact, rtol=1e-5, atol=1e-4, err_msg=f"rank {rank}")
+
+
+def _tp_exchange_worker(rank, world, port, q):
+    """Row split with an injected exchange (the shape of p2p.PeerRowGemv):
+    batch-1 inputs go to the exchange, batch > 1 to the GEMV + all-reduce."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n, k = 64, 512
+        w = synth.q4_0_weight(n, k, seed=21)
+        kl = k // world
+        shard = tp.split_k_gguf(w, k, "q4_0", rank, world)
+
+        def local(wt, xx, nn, kk):
+            w16 = oracle.dequant_q4_0(wt.numpy()).reshape(nn, kk)
+            return torch.from_numpy((xx.float().numpy() @ w16.astype(np.float32).T).astype(np.float32))
+
+        calls = []
+
+        def exchange(fmt, wt, x_local, nn, kk, out=None):  # CPU stand-in for the fused kernel
+            calls.append((fmt, tuple(x_local.shape), nn, kk))
+            y = local(wt, x_local, nn, kk)
+            dist.all_reduce(y)
+            return y
+
+        row = tp.RowParallelGemv((shard,), n, k, "q4_0", rank, world, exchange=exchange,
+                                 gemv=lambda wt, xx, nn, kk, out=None: local(wt[0], xx, nn, kk))
+        x1 = synth.activations(1, k, seed=22)
+        x2 = synth.activations(2, k, seed=23)
+        y1 = row(x1[:, rank * kl:(rank + 1) * kl].contiguous())
+        y2 = row(x2[:, rank * kl:(rank + 1) * kl].contiguous())
+        q.put((rank, y1.numpy(), y2.numpy(), calls))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_routes_batch_one_to_the_exchange():
+    out = _run(_tp_exchange_worker)
+    n, k = 64, 512
+    w16 = oracle.dequant_q4_0(synth.q4_0_weight(n, k, seed=21).numpy()).reshape(n, k)
+    e1 = oracle.gemv_exact(w16, synth.activations(1, k, seed=22).numpy())
+    e2 = oracle.gemv_exact(w16, synth.activations(2, k, seed=23).numpy())
+    for rank, y1, y2, calls in out:
+        assert calls == [("q4_0", (1, k // 2), n, k // 2)], calls   # batch 2 took the all-reduce path
+        np.testing.assert_allclose(y1, e1, rtol=1e-5, atol=1e-4, err_msg=f"rank {rank}")
+        np.testing.assert_allclose(y2, e2, rtol=1e-5, atol=1e-4, err_msg=f"rank {rank}")
