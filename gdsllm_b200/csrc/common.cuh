@@ -26,6 +26,10 @@ __device__ int g_device_error;
 // Upper bound for any wait on an async copy, in nanoseconds of %globaltimer.
 // A weight tile takes microseconds to arrive; one second means "never".
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+// Waits on another GPU (peer all-reduces, the row-split GEMV's finishers)
+// take their bound from a launch parameter instead, by default this value
+// (gdsq_set_peer_wait_limit_ns changes it for later launches).
+constexpr unsigned long long kPeerWaitDefaultNs = kWaitLimitNs;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

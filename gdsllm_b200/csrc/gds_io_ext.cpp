@@ -355,6 +355,14 @@ torch::Tensor view_of(const Handle& h, std::vector<int64_t> shape, const std::st
 torch::Tensor py_view_tensor(Handle h, std::vector<int64_t> shape, const std::string& dtype,
                              int64_t offset) {
   require_handle(h, "py_view_tensor");
+  // The view must lie inside the buffer: offset + numel * element size.
+  int64_t numel = 1;
+  for (int64_t d : shape) {
+    if (d < 0) throw std::runtime_error("py_view_tensor: negative dimension " + std::to_string(d));
+    numel *= d;
+  }
+  const int64_t elem = static_cast<int64_t>(c10::elementSize(parse_dtype(dtype)));
+  require_range(h, offset, numel * elem, "py_view_tensor", "view");
   return view_of(h, std::move(shape), dtype, offset);
 }
 

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -18,7 +19,6 @@
 #include "common.cuh"
 #include "dequant.cuh"
 #include "gemv.cuh"
-#include "gemv_tc.cuh"
 #include "gemv_tcb.cuh"
 #include "moe.cuh"
 #include "p2p.cuh"
@@ -28,6 +28,7 @@ namespace {
 
 thread_local std::string t_last_error;
 int g_pdl_enabled = 0;
+std::atomic<unsigned long long> g_peer_wait_ns{kPeerWaitDefaultNs};
 
 int fail(int status, const char* fmt, ...) {
   char buf[512];
@@ -371,12 +372,37 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, L.total);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     if (occ < 1) continue;
+    if (const char* cap = getenv("GDSQ_GEMV_OCC")) {  // tuning sweeps: CTAs per SM per launch, at most
+      const int v = atoi(cap);
+      if (v >= 1 && v < occ) occ = v;
+    }
     const long long slots = (long long)dev.sms * occ;
     out->cs = c.cs;
     out->stages = c.st;
     out->copy = c.cp;
     out->nclusters = (long long)R * c.cs <= slots ? R : (int)(slots / c.cs);
     out->smem = L.total;
+    if (TP && c.cs > 1) {
+      // The finisher CTAs wait for rows of every other cluster, so the whole
+      // grid must be resident at once: cap the clusters at what the GPU can
+      // hold together (cluster placement can allow fewer than slots / cs).
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(out->nclusters * c.cs);
+      cfg.blockDim = dim3(kGemvWarps * 32);
+      cfg.dynamicSmemBytes = L.total;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = c.cs;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int max_clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (max_clusters < 1) continue;
+      if (out->nclusters > max_clusters) out->nclusters = max_clusters;
+    }
     return GDSQ_OK;
   }
   return fail(GDSQ_ERR_UNSUPPORTED, "no GEMV launch plan fits shared memory");
@@ -479,97 +505,6 @@ int launch_fast_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t s
     case 8: return launch_fast<F, 8, GS>(p, dev, stream);
     default: return launch_fast<F, 16, GS>(p, dev, stream);
   }
-}
-
-// Tensor-core Q4_0 GEMV (batch 1), opt-in with GDSQ_GEMV_TC=1: correct, but
-// on B200 its per-pair dequant -> MMA -> commit round trip makes it slower
-// than the CUDA-core kernel on the decode shapes, so it is not the default.
-bool tc_enabled() {
-  const char* e = getenv("GDSQ_GEMV_TC");
-  return e && e[0] == '1';
-}
-
-int launch_tc_q4_0(GemvParams p, const DeviceInfo& dev, cudaStream_t stream) {
-  const int R = (p.N + kTcRows - 1) / kTcRows;
-  const int C = p.K / kChunkCols;
-  auto kernel = gemv_tc_q4_0_kernel;
-  int force_cs = 0, force_st = 0, force_cp = 0;
-  const bool forced = plan_override(&force_cs, &force_st, &force_cp);
-  // Largest cluster (<= 8, >= 2 chunks per CTA) whose grid still fits the
-  // GPU in one wave at the occupancy its shared memory allows; 2 stages.
-  int cs = 1, stages = 2;
-  const uint64_t key = ((uint64_t)1 << 62) | ((uint64_t)(unsigned)p.N << 22) | (uint64_t)(unsigned)(p.K / 32);
-  bool cached = false;
-  if (!forced) {
-    std::lock_guard<std::mutex> lock(g_plan_mutex);
-    auto it = g_plans[dev.ordinal].find(key);
-    if (it != g_plans[dev.ordinal].end()) {
-      cs = it->second.cs;
-      stages = it->second.stages;
-      cached = true;
-    }
-  }
-  if (forced) {
-    cs = force_cs;
-    stages = force_st < 2 ? 2 : force_st;
-  } else if (!cached) {
-    const int cs_max = C / 2 < 1 ? 1 : (C / 2 > kMaxCluster ? kMaxCluster : C / 2);
-    for (int c = cs_max; c >= 1; --c) {
-      const TcLayout Lc = tc_layout(p.K, c, stages);
-      if (Lc.total > dev.smem_optin) continue;
-      cudaError_t e = ensure_smem(kernel, Lc.total, dev.ordinal);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tc)");
-      int occ = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kTcThreads, Lc.total);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-      if ((long long)R * c <= (long long)dev.sms * occ) {
-        cs = c;
-        break;
-      }
-    }
-  }
-  if (!forced && !cached) {
-    GemvPlan plan;
-    plan.cs = cs;
-    plan.stages = stages;
-    std::lock_guard<std::mutex> lock(g_plan_mutex);
-    g_plans[dev.ordinal][key] = plan;
-  }
-  const TcLayout L = tc_layout(p.K, cs, stages);
-  if (L.total > dev.smem_optin) return fail(GDSQ_ERR_UNSUPPORTED, "tensor-core GEMV does not fit shared memory");
-  CUtensorMap wmap;
-  int mst = weight_map<kFmtQ4_0>(dev, p.w, p.N, p.row_bytes, &wmap, kTcRows);
-  if (mst != GDSQ_OK) return mst;
-  cudaError_t e = ensure_smem(kernel, L.total, dev.ordinal);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv tc)");
-  p.cs = cs;
-  p.stages = stages;
-  p.copy = 1;
-  p.num_rg = R;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(R * cs);
-  cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = L.total;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (cs > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = cs;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  if (g_pdl_enabled) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
-  if (e != cudaSuccess) return cuda_fail(e, "gemv tc launch");
-  return GDSQ_OK;
 }
 
 // Tensor-core batched GEMV (gemv_tcb.cuh): default for batch >= 5, where
@@ -796,6 +731,7 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
     }
     p.tp_own_buf = p.tp_bufs[tp->rank];
     p.tp_own_flags = p.tp_flags[tp->rank];
+    p.tp_wait_ns = g_peer_wait_ns.load();
     if (fmt == kFmtQ4_0) return launch_fast<kFmtQ4_0, 1, 0, true>(p, *dev, stream);
     return launch_fast<kFmtQ8_0, 1, 0, true>(p, *dev, stream);
   }
@@ -813,7 +749,6 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
     }
   }
   if (fmt == kFmtQ4_0) {
-    if (shape_ok && batch == 1 && tc_enabled()) return launch_tc_q4_0(p, *dev, stream);
     if (shape_ok && fast_min_smem<kFmtQ4_0>(batch, in_dim, 0) <= dev->smem_optin)
       return launch_fast_batch<kFmtQ4_0, 0>(p, *dev, stream);
     return launch_generic<kFmtQ4_0>(p, stream);
@@ -1132,6 +1067,10 @@ int gdsq_set_pdl(int enable) {
   return GDSQ_OK;
 }
 
+unsigned long long gdsq_set_peer_wait_limit_ns(unsigned long long ns) {
+  return g_peer_wait_ns.exchange(ns == 0 ? kPeerWaitDefaultNs : ns);
+}
+
 int gdsq_device_error(int device, int clear, int* out_bits) {
   t_last_error.clear();
   if (!out_bits) return fail(GDSQ_ERR_INVALID_VALUE, "gdsq_device_error: null output");
@@ -1353,14 +1292,24 @@ void* g_moe_h_addr[kMaxDevices];
 bool g_moe_h_ready[kMaxDevices];
 
 // Device address of the array on the current device, looked up once per
-// device (with that device current) and cached.
-int moe_h_scratch(void** out) {
+// device (with that device current) and cached.  The lookup may not run
+// while `stream` is being captured into a CUDA graph, so a first call made
+// during a capture is rejected with a message saying so.
+int moe_h_scratch(cudaStream_t stream, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(GDSQ_ERR_UNSUPPORTED, "device %d", dev);
   std::lock_guard<std::mutex> lock(g_device_mutex);
   if (!g_moe_h_ready[dev]) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    if (cap != cudaStreamCaptureStatusNone)
+      return fail(GDSQ_ERR_INVALID_VALUE,
+                  "moe noalloc: the first call on device %d must come before any stream capture (it looks up the "
+                  "static scratch's address once); make one uncaptured call first",
+                  dev);
     void* addr = nullptr;
     e = cudaGetSymbolAddress(&addr, g_moe_h_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(MoE scratch)");
@@ -1388,6 +1337,18 @@ int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales,
                                int expert_count, int expert_total, int flags, void* stream) {
   t_last_error.clear();
   const bool shared = shared_gate_weight != nullptr;
+  // Both stages must agree on the shared expert: gate/up writes top_k + 1
+  // slots per token into the scratch when it is present, and down reads as
+  // many.  So its gate, up and down tensors and its weights are all given or
+  // all null.
+  const void* shared_ptrs[] = {shared_gate_weight, shared_gate_scales, shared_gate_biases, shared_up_weight,
+                               shared_up_scales,   shared_up_biases,   shared_down_weight, shared_down_scales,
+                               shared_down_biases, shared_weights};
+  for (const void* q : shared_ptrs)
+    if ((q != nullptr) != shared)
+      return fail(GDSQ_ERR_INVALID_VALUE,
+                  "moe noalloc: the shared expert's gate, up and down tensors and shared_weights must be all "
+                  "given or all null");
   const long long need = (long long)num_tokens * (top_k + (shared ? 1 : 0)) * inter_dim;
   if (num_tokens < 0 || top_k < 1 || inter_dim <= 0)
     return fail(GDSQ_ERR_INVALID_VALUE, "moe noalloc: num_tokens %d, top_k %d, inter_dim %d", num_tokens, top_k,
@@ -1399,7 +1360,7 @@ int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales,
                 num_tokens, top_k + (shared ? 1 : 0), inter_dim, need, kNoAllocHElems);
   if (num_tokens == 0) return GDSQ_OK;
   void* h = nullptr;
-  int st = moe_h_scratch(&h);
+  int st = moe_h_scratch(static_cast<cudaStream_t>(stream), &h);
   if (st != GDSQ_OK) return st;
   st = gdsq_moe_affine_q4_gate_up(gate_weight, gate_scales, gate_biases, up_weight, up_scales, up_biases,
                                   shared_gate_weight, shared_gate_scales, shared_gate_biases, shared_up_weight,
@@ -1438,6 +1399,7 @@ int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* 
   a.cap = cap;
   a.rank = rank;
   a.world = world;
+  a.wait_ns = g_peer_wait_ns.load();
   const int grid = (n + kP2PElemsPerCta - 1) / kP2PElemsPerCta;
   cudaError_t e = launch(allreduce_oneshot_kernel, dim3(grid), dim3(kP2PThreads), 0,
                          static_cast<cudaStream_t>(stream_v), g_pdl_enabled != 0, a);
@@ -1474,6 +1436,7 @@ int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, co
   a.cap = cap;
   a.rank = rank;
   a.world = world;
+  a.wait_ns = g_peer_wait_ns.load();
   const int grid = (n + kLLElemsPerCta - 1) / kLLElemsPerCta;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   cudaError_t e = elem_type == GDSQ_ELEM_F32

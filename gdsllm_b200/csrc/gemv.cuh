@@ -22,9 +22,10 @@
 //   * The activations of the CTA's K slice are staged once in shared memory,
 //     permuted so that pair order matches the dequantizer's output order; all
 //     32 lanes read the same address, so activation loads are broadcasts.
-//   * Nibbles become exact fp16 (q - 8) with the magic-number trick; products
-//     are summed in fp16 pairs over at most 16 terms per 32-column block and
-//     then in fp32.  Q8_0 is dequantized straight to fp32 and summed in fp32.
+//   * Arithmetic is fp32 throughout, as in the reference: every product of a
+//     quantized value and an activation is exact in fp32 and every sum is an
+//     fp32 sum (see "Exact fp32 products" below for how the packed values
+//     reach the FMA without a conversion instruction each).
 //   * Per row group: warps meet in shared memory; with cs > 1 every CTA writes
 //     its partial sums into the cluster leader's shared memory (distributed
 //     shared memory), and after a cluster barrier the leader adds the cs
@@ -53,12 +54,16 @@ struct GemvFormat;
 // 16-byte loads of 8 consecutive lanes hit 8 distinct bank groups.  The
 // affine pitch is 128 bytes, so its boxes use the 128-byte swizzle (16-byte
 // unit u of row r is stored at unit u ^ (r % 8)).
+// Activations are staged as scaled fp32 (kXBytes per column) in the order the
+// dequantizer emits its values, plus one fp32 per 32-column block (GGUF
+// formats: the block's offset term) or per quantization group (affine: the
+// group's activation sum).
 template <>
 struct GemvFormat<kFmtQ4_0> {
   static constexpr int kChunkBytes = 144;  // 8 blocks x 18 B
   static constexpr int kMaxCopyChunks = 2;  // chunks (TMA boxes) per ring stage, at most
   static constexpr bool kSwizzle = false;
-  static constexpr int kXBytes = 2;        // activations kept as permuted fp16
+  static constexpr int kXBytes = 4;
 };
 
 template <>
@@ -66,7 +71,7 @@ struct GemvFormat<kFmtQ8_0> {
   static constexpr int kChunkBytes = 272;  // 8 blocks x 34 B
   static constexpr int kMaxCopyChunks = 1;
   static constexpr bool kSwizzle = false;
-  static constexpr int kXBytes = 4;        // activations kept as fp32
+  static constexpr int kXBytes = 4;
 };
 
 template <>
@@ -74,8 +79,54 @@ struct GemvFormat<kFmtAffineQ4> {
   static constexpr int kChunkBytes = 128;  // 32 words of 8 nibbles
   static constexpr int kMaxCopyChunks = 2;
   static constexpr bool kSwizzle = true;
-  static constexpr int kXBytes = 2;
+  static constexpr int kXBytes = 4;
 };
+
+// ---------------------------------------------------------------------------
+// Exact fp32 products from packed integers.
+//
+// A field of a 32-bit word masked in place, v << s with v < 2^m and
+// s + m <= 23, read as fp32 bits is the subnormal v * 2^(s - 149): an exact
+// value, produced by one LOP3 and consumed by the FMA at full rate (this
+// library is built without flush-to-zero).  The staging code multiplies the
+// activation that meets field position s by 2^(110 - s), so every product is
+// exactly v * x * 2^-39 and the running sums are ordinary fp32 sums in units
+// of 2^-39; the epilogue multiplies by 2^39, which is exact.  Range: fp16
+// |x| <= 65504 < 2^16 keeps x * 2^110 below 2^126, and the smallest nonzero
+// product (x = 2^-24, v = 1) is 2^-63, a normal fp32.
+//
+// Nibble words (Q4_0 and affine) give 4 fp32 pairs per word, the FFMA2
+// operand pairs: (bits 0-3, 4-7), (8-11, 12-15), (16-19, 20-23), (24-27,
+// 28-31), built as q & 0xF, q & 0xF0, q & 0xF00, q & 0xF000, q & 0xF0000,
+// (q >> 16) & 0xF0, (q >> 16) & 0xF00, q >> 28 — field shifts s = 0, 4, 8,
+// 12, 16, 4, 8, 0.  Byte words (Q8_0, excess-128) give 2 pairs: u & 0xFF,
+// u & 0xFF00, (u >> 16) & 0xFF, (u >> 16) & 0xFF00 — shifts 0, 8, 0, 8.
+constexpr float kUnscale = 0x1p39f;
+
+// Activation scale for each of the 8 nibble fields of a word, in word order.
+__device__ __forceinline__ float nib_xscale(int k) {
+  return k == 0 || k == 7 ? 0x1p110f : k == 1 || k == 5 ? 0x1p106f : k == 2 || k == 6 ? 0x1p102f
+         : k == 3 ? 0x1p98f : 0x1p94f;
+}
+
+__device__ __forceinline__ void nib_fields(uint32_t q, float2 (&f)[4]) {
+  const uint32_t h = q >> 16;
+  f[0] = make_float2(__uint_as_float(q & 0xFu), __uint_as_float(q & 0xF0u));
+  f[1] = make_float2(__uint_as_float(q & 0xF00u), __uint_as_float(q & 0xF000u));
+  f[2] = make_float2(__uint_as_float(q & 0xF0000u), __uint_as_float(h & 0xF0u));
+  f[3] = make_float2(__uint_as_float(h & 0xF00u), __uint_as_float(q >> 28));
+}
+
+// Signed bytes as excess-128 fields (value + 128).
+__device__ __forceinline__ void byte_fields(uint32_t q, float2 (&f)[2]) {
+  const uint32_t u = q ^ 0x80808080u;
+  const uint32_t h = u >> 16;
+  f[0] = make_float2(__uint_as_float(u & 0xFFu), __uint_as_float(u & 0xFF00u));
+  f[1] = make_float2(__uint_as_float(h & 0xFFu), __uint_as_float(h & 0xFF00u));
+}
+
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
 
 // Bytes of one ring stage holding `copy` chunks of 32 rows.
 template <int F>
@@ -118,6 +169,7 @@ struct GemvParams {
   int* tp_flags[8];
   unsigned long long* tp_own_buf;  // tp_bufs[tp_rank]
   int* tp_own_flags;               // tp_flags[tp_rank]
+  unsigned long long tp_wait_ns;   // bound of the finishers' wait for the peers' rows
 };
 
 constexpr int kMaxGroup = 4;
@@ -173,7 +225,8 @@ __device__ __forceinline__ void tp_publish(const GemvParams& p, int e, int rg, i
 // parameter block is never copied to local memory for the call.  Returns
 // false if a wait expired.
 __device__ __noinline__ bool tp_finish_cta(const unsigned long long* buf, int* own, __half* y, int N, int num_rg,
-                                           int world, int rows_cap, int e, int f, int nf) {
+                                           int world, int rows_cap, int e, int f, int nf,
+                                           unsigned long long wait_ns) {
   __shared__ int s_fail;
   constexpr int kRows = 8;  // rows per thread per pass
   if (threadIdx.x == 0) s_fail = 0;
@@ -201,7 +254,7 @@ __device__ __noinline__ bool tp_finish_cta(const unsigned long long* buf, int* o
         const int row = base + j * blockDim.x;
         while (ok && (int)(w[j] >> 32) != e) {
           if (t0 == 0) t0 = global_timer_ns();
-          else if (global_timer_ns() - t0 > kWaitLimitNs) {
+          else if (global_timer_ns() - t0 > wait_ns) {
             record_device_error(kDevErrBarrierTimeout);
             ok = false;
             break;
@@ -254,10 +307,12 @@ __host__ __device__ inline GemvSmemLayout gemv_smem_layout(int B, int K, int gro
   off += kGemvWarps * stages * stage_bytes<F>(copy);
   L.xs = off;
   off += B * L.kslice * T::kXBytes;
-  L.xsum = off;
-  L.sb = off;
+  L.xsum = off;  // one fp32 per block (GGUF) or per group (affine) and batch row
   L.sb_stride = 0;
-  if (F == kFmtAffineQ4) {
+  if (F != kFmtAffineQ4) {
+    off += B * (L.kslice / 32) * 4;
+    L.sb = off;
+  } else {
     const int gs = L.kslice / group;
     off += B * gs * 4;
     L.sb = off;
@@ -276,66 +331,103 @@ __host__ __device__ inline GemvSmemLayout gemv_smem_layout(int B, int K, int gro
 // Activation staging: columns [col0, col0 + ncols) of x into shared memory,
 // row stride ncols_max.  Runs after the programmatic-dependency wait.
 
-// Q4_0: per 32-column block, 16 half2 in the order the dequantizer emits:
-// for qs word i (bytes 4i..4i+3):
-//   (x[4i], x[4i+2]), (x[16+4i], x[18+4i]), (x[4i+1], x[4i+3]), (x[17+4i], x[19+4i])
-__device__ __forceinline__ void stage_x_q4_0(const __half* __restrict__ x, uint8_t* xs, int nb,
-                                             int B, int K, int col0, int ncols, int ld) {
+// Every staging function works in units of 8 columns (one thread each, a
+// warp's units consecutive) and writes, per unit, 8 scaled fp32 activations
+// as two 16-byte stores; `ld` is the staged row stride in columns.  Units of
+// batch rows >= nb are zero.
+
+__device__ __forceinline__ void store_x8(uint8_t* xs, size_t col, const float (&v)[8]) {
+  float4* dst = reinterpret_cast<float4*>(xs + col * 4);
+  dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+  dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ void h8_to_f32(uint2 a, uint2 b, float (&v)[8]) {
+  const float2 p0 = __half22float2(u32_as_h2(a.x)), p1 = __half22float2(u32_as_h2(a.y));
+  const float2 p2 = __half22float2(u32_as_h2(b.x)), p3 = __half22float2(u32_as_h2(b.y));
+  v[0] = p0.x; v[1] = p0.y; v[2] = p1.x; v[3] = p1.y;
+  v[4] = p2.x; v[5] = p2.y; v[6] = p3.x; v[7] = p3.y;
+}
+
+// Q4_0: unit (b, block, i) stages the 8 columns that meet qs word i (bytes
+// 4i..4i+3) in field order: x[4i], x[4i+16], x[4i+1], x[4i+17], x[4i+2],
+// x[4i+18], x[4i+3], x[4i+19], each times nib_xscale(field).  xc[b][block] =
+// -8 * sum(x over the block) * 2^-39, the (q - 8) offset of the block in the
+// units of the partial sums.
+__device__ __forceinline__ void stage_x_q4_0(const __half* __restrict__ x, uint8_t* xs, float* xc,
+                                             int nb, int B, int K, int col0, int ncols, int ld) {
   const int nblk = ncols / 32;
-  for (int u = threadIdx.x; u < B * nblk; u += blockDim.x) {
-    const int b = u / nblk;
-    const int blk = u - b * nblk;
-    uint4* dst = reinterpret_cast<uint4*>(xs + ((size_t)b * ld + blk * 32) * 2);
-    if (b >= nb) {
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      dst[0] = z; dst[1] = z; dst[2] = z; dst[3] = z;
-      continue;
-    }
-    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + blk * 32);
-    uint32_t h[16];
+  const int total = B * nblk * 4;
+  for (int base = threadIdx.x & ~31; base < total; base += blockDim.x) {
+    const int u = base + (threadIdx.x & 31);
+    float s = 0.f;
+    int b = 0, blk = 0, i = 0;
+    if (u < total) {
+      i = u & 3;
+      blk = (u >> 2) % nblk;
+      b = (u >> 2) / nblk;
+      float v[8];
+      if (b < nb) {
+        const __half* xb = x + (size_t)b * K + col0 + blk * 32 + 4 * i;
+        float lo[8];
+        h8_to_f32(*reinterpret_cast<const uint2*>(xb), *reinterpret_cast<const uint2*>(xb + 16), lo);
+        // lo = x[4i..4i+3], x[4i+16..4i+19]
+        const float o[8] = {lo[0], lo[4], lo[1], lo[5], lo[2], lo[6], lo[3], lo[7]};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 v = src[j];
-      h[4 * j] = v.x; h[4 * j + 1] = v.y; h[4 * j + 2] = v.z; h[4 * j + 3] = v.w;
-    }
+        for (int k = 0; k < 8; ++k) {
+          v[k] = o[k] * nib_xscale(k);
+          s += o[k];
+        }
+      } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 o;
-      o.x = __byte_perm(h[2 * i], h[2 * i + 1], 0x5410);          // x[4i],    x[4i+2]
-      o.y = __byte_perm(h[8 + 2 * i], h[9 + 2 * i], 0x5410);      // x[16+4i], x[18+4i]
-      o.z = __byte_perm(h[2 * i], h[2 * i + 1], 0x7632);          // x[4i+1],  x[4i+3]
-      o.w = __byte_perm(h[8 + 2 * i], h[9 + 2 * i], 0x7632);      // x[17+4i], x[19+4i]
-      dst[i] = o;
+        for (int k = 0; k < 8; ++k) v[k] = 0.f;
+      }
+      store_x8(xs, (size_t)b * ld + blk * 32 + 8 * i, v);
     }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (u < total && i == 0) xc[b * (ld / 32) + blk] = s * (-8.0f * 0x1p-39f);
   }
 }
 
-// Q8_0: plain fp32 copy of x.
-__device__ __forceinline__ void stage_x_f32(const __half* __restrict__ x, uint8_t* xs, int nb,
-                                            int B, int K, int col0, int ncols, int ld) {
+// Q8_0: unit (b, j) stages columns 8j..8j+7 in order, scaled 2^110, 2^102
+// alternately (byte fields at shifts 0 and 8); xc[b][block] = -128 *
+// sum(x over the block) * 2^-39 (the excess-128 offset).
+__device__ __forceinline__ void stage_x_q8_0(const __half* __restrict__ x, uint8_t* xs, float* xc,
+                                             int nb, int B, int K, int col0, int ncols, int ld) {
   const int n8 = ncols / 8;
-  for (int u = threadIdx.x; u < B * n8; u += blockDim.x) {
-    const int b = u / n8;
-    const int j = u - b * n8;
-    float4* dst = reinterpret_cast<float4*>(xs + ((size_t)b * ld + j * 8) * 4);
-    if (b >= nb) {
-      dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-      dst[1] = dst[0];
-      continue;
+  const int total = B * n8;
+  for (int base = threadIdx.x & ~31; base < total; base += blockDim.x) {
+    const int u = base + (threadIdx.x & 31);
+    float s = 0.f;
+    int b = 0, j = 0;
+    if (u < total) {
+      b = u / n8;
+      j = u - b * n8;
+      float v[8];
+      if (b < nb) {
+        const uint4 h = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
+        h8_to_f32(make_uint2(h.x, h.y), make_uint2(h.z, h.w), v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          s += v[k];
+          v[k] *= (k & 1) ? 0x1p102f : 0x1p110f;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = 0.f;
+      }
+      store_x8(xs, (size_t)b * ld + j * 8, v);
     }
-    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
-    const float2 a = __half22float2(u32_as_h2(v.x));
-    const float2 c = __half22float2(u32_as_h2(v.y));
-    const float2 e = __half22float2(u32_as_h2(v.z));
-    const float2 g = __half22float2(u32_as_h2(v.w));
-    dst[0] = make_float4(a.x, a.y, c.x, c.y);
-    dst[1] = make_float4(e.x, e.y, g.x, g.y);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (u < total && (j & 3) == 0) xc[b * (ld / 32) + j / 4] = s * (-128.0f * 0x1p-39f);
   }
 }
 
-// Affine: per 8-column word, (x0,x4),(x1,x5),(x2,x6),(x3,x7); plus the fp32
-// sum of x over each quantization group (needed for the bias term), stored
-// at xsum[b * (ld / GS) + group].
+// Affine: unit (b, j) stages word j's columns 8j..8j+7 in order, each times
+// nib_xscale(field); xsum[b][group] = sum(x over the group) * 2^-39 (the
+// bias term, in the units of the partial sums).
 template <int GS>
 __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uint8_t* xs,
                                                float* xsum, int nb, int B, int K, int col0,
@@ -350,24 +442,24 @@ __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uin
     if (u < total) {
       b = u / n8;
       j = u - b * n8;
-      uint4 o = make_uint4(0, 0, 0, 0);
+      float v[8];
       if (b < nb) {
-        const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
-        o.x = __byte_perm(v.x, v.z, 0x5410);  // x0, x4
-        o.y = __byte_perm(v.x, v.z, 0x7632);  // x1, x5
-        o.z = __byte_perm(v.y, v.w, 0x5410);  // x2, x6
-        o.w = __byte_perm(v.y, v.w, 0x7632);  // x3, x7
-        const float2 a = __half22float2(u32_as_h2(v.x));
-        const float2 c = __half22float2(u32_as_h2(v.y));
-        const float2 e = __half22float2(u32_as_h2(v.z));
-        const float2 g = __half22float2(u32_as_h2(v.w));
-        s = ((a.x + a.y) + (c.x + c.y)) + ((e.x + e.y) + (g.x + g.y));
+        const uint4 h = *reinterpret_cast<const uint4*>(x + (size_t)b * K + col0 + j * 8);
+        h8_to_f32(make_uint2(h.x, h.y), make_uint2(h.z, h.w), v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          s += v[k];
+          v[k] *= nib_xscale(k);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = 0.f;
       }
-      *reinterpret_cast<uint4*>(xs + ((size_t)b * ld + j * 8) * 2) = o;
+      store_x8(xs, (size_t)b * ld + j * 8, v);
     }
 #pragma unroll
     for (int m = 1; m < kLanesPerGroup; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-    if (u < total && (j % kLanesPerGroup) == 0) xsum[b * (ld / GS) + j / kLanesPerGroup] = s;
+    if (u < total && (j % kLanesPerGroup) == 0) xsum[b * (ld / GS) + j / kLanesPerGroup] = s * 0x1p-39f;
   }
 }
 
@@ -375,11 +467,12 @@ __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uin
 // Per-chunk compute: one lane, one row, 256 columns.  `src` is the shared
 // address of this lane's chunk bytes, `xa` the shared address of the staged
 // activations of this chunk for batch row 0 and `xb` the byte distance
-// between batch rows.
+// between batch rows; `xc` / `xcb` likewise for the per-block offset terms
+// (GGUF formats).  acc[] accumulates in units of 2^-39.
 
 template <int B>
-__device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t xb,
-                                           float (&acc)[B]) {
+__device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t xb, uint32_t xc,
+                                           uint32_t xcb, float (&acc)[B]) {
   uint32_t w[36];
 #pragma unroll
   for (int j = 0; j < 9; ++j) {
@@ -402,31 +495,32 @@ __device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t x
       for (int i = 0; i < 4; ++i) q[i] = w[wi + 1 + i];
     }
     const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(d16)));
-    __half2 wv[16];
+    float2 f[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) unpack_nibbles_minus8(q[i], &wv[4 * i]);
+    for (int i = 0; i < 4; ++i) nib_fields(q[i], f[i]);
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      // four independent fp16 chains of 4 products each
-      __half2 a[4];
+      // sum of n * x over the block (two fp32 FFMA2 chains), then the -8 offset
+      float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint4 xv = lds128(xa + b * xb + (blk * 4 + i) * 16);
-        a[i] = __hmul2(wv[4 * i + 0], u32_as_h2(xv.x));
-        a[i] = __hfma2(wv[4 * i + 1], u32_as_h2(xv.y), a[i]);
-        a[i] = __hfma2(wv[4 * i + 2], u32_as_h2(xv.z), a[i]);
-        a[i] = __hfma2(wv[4 * i + 3], u32_as_h2(xv.w), a[i]);
+        const uint32_t xw = xa + b * xb + (blk * 32 + i * 8) * 4;
+        const float4 x0 = lds128f(xw);
+        const float4 x1 = lds128f(xw + 16);
+        s0 = __ffma2_rn(f[i][0], lo2(x0), s0);
+        s1 = __ffma2_rn(f[i][1], hi2(x0), s1);
+        s0 = __ffma2_rn(f[i][2], lo2(x1), s0);
+        s1 = __ffma2_rn(f[i][3], hi2(x1), s1);
       }
-      const float2 f = __half22float2(__hadd2(__hadd2(a[0], a[1]), __hadd2(a[2], a[3])));
-      acc[b] = fmaf(d, f.x + f.y, acc[b]);
+      const float sum = ((s0.x + s0.y) + (s1.x + s1.y)) + lds32f(xc + b * xcb + blk * 4);
+      acc[b] = fmaf(d, sum, acc[b]);
     }
   }
 }
 
 template <int B>
-__device__ __forceinline__ void chunk_q8_0(uint32_t src, uint32_t xa, uint32_t xb,
-                                           float (&acc)[B]) {
-  constexpr float kBias = 8388736.0f;  // 2^23 + 128
+__device__ __forceinline__ void chunk_q8_0(uint32_t src, uint32_t xa, uint32_t xb, uint32_t xc,
+                                           uint32_t xcb, float (&acc)[B]) {
   // Two blocks (68 bytes) at a time: words [17*pr, 17*pr + 17) of the chunk.
 #pragma unroll
   for (int pr = 0; pr < 4; ++pr) {
@@ -453,35 +547,35 @@ __device__ __forceinline__ void chunk_q8_0(uint32_t src, uint32_t xa, uint32_t x
         for (int i = 0; i < 8; ++i) q[i] = w[sh + 9 + i];
       }
       const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(d16)));
-      float wf[32];
+      float2 f[8][2];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t u = q[i] ^ 0x80808080u;  // int8 -> excess-128
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          wf[4 * i + k] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + k)) - kBias;
-      }
+      for (int i = 0; i < 8; ++i) byte_fields(q[i], f[i]);
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        // sum of (v + 128) * x over the block, then the -128 offset
+        float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float4 xv = lds128f(xa + b * xb + (blk * 8 + i) * 16);
-          s[i & 3] = fmaf(wf[4 * i + 0], xv.x, s[i & 3]);
-          s[i & 3] = fmaf(wf[4 * i + 1], xv.y, s[i & 3]);
-          s[i & 3] = fmaf(wf[4 * i + 2], xv.z, s[i & 3]);
-          s[i & 3] = fmaf(wf[4 * i + 3], xv.w, s[i & 3]);
+          if (i & 1) {
+            s1 = __ffma2_rn(f[i][0], lo2(xv), s1);
+            s1 = __ffma2_rn(f[i][1], hi2(xv), s1);
+          } else {
+            s0 = __ffma2_rn(f[i][0], lo2(xv), s0);
+            s0 = __ffma2_rn(f[i][1], hi2(xv), s0);
+          }
         }
-        acc[b] = fmaf(d, (s[0] + s[1]) + (s[2] + s[3]), acc[b]);
+        const float sum = ((s0.x + s0.y) + (s1.x + s1.y)) + lds32f(xc + b * xcb + blk * 4);
+        acc[b] = fmaf(d, sum, acc[b]);
       }
     }
   }
 }
 
-// Affine: sum_k (n_k*s + b) x_k = s * sum_k (n_k - 8) x_k + (b + 8 s) * sum_k x_k
-// over each group; the (n - 8) form keeps the fp16 partial sums small.
-// `sb_row` (shared address of this lane's (scale, bias) row) and `xsum` are
-// indexed by the group's position in the K slice, starting at g0.
+// Affine: sum_k (n_k*s + b) x_k = s * sum_k n_k x_k + b * sum_k x_k over each
+// group, both sums fp32.  `sb_row` (shared address of this lane's (scale,
+// bias) row) and `xsum` are indexed by the group's position in the K slice,
+// starting at g0.
 template <int B, int GS>
 __device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_t xa, uint32_t xb,
                                              uint32_t xsum, uint32_t xsum_b, uint32_t sb_row,
@@ -496,36 +590,30 @@ __device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_
   constexpr int kWordsPerGroup = GS / 8;
 #pragma unroll
   for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
-    float P[B];
+    float2 s0[B], s1[B];
 #pragma unroll
-    for (int b = 0; b < B; ++b) P[b] = 0.f;
+    for (int b = 0; b < B; ++b) s0[b] = s1[b] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int sub = 0; sub < kWordsPerGroup / 4; ++sub) {
-      __half2 wv[16];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) unpack_nibbles_minus8(w[gi * kWordsPerGroup + sub * 4 + t], &wv[4 * t]);
+    for (int t = 0; t < kWordsPerGroup; ++t) {
+      float2 f[4];
+      nib_fields(w[gi * kWordsPerGroup + t], f);
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        __half2 a[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint4 xv = lds128(xa + b * xb + (gi * kWordsPerGroup + sub * 4 + t) * 16);
-          a[t] = __hmul2(wv[4 * t + 0], u32_as_h2(xv.x));
-          a[t] = __hfma2(wv[4 * t + 1], u32_as_h2(xv.y), a[t]);
-          a[t] = __hfma2(wv[4 * t + 2], u32_as_h2(xv.z), a[t]);
-          a[t] = __hfma2(wv[4 * t + 3], u32_as_h2(xv.w), a[t]);
-        }
-        const float2 f = __half22float2(__hadd2(__hadd2(a[0], a[1]), __hadd2(a[2], a[3])));
-        P[b] += f.x + f.y;
+        const uint32_t xw = xa + b * xb + (gi * GS + t * 8) * 4;
+        const float4 x0 = lds128f(xw);
+        const float4 x1 = lds128f(xw + 16);
+        s0[b] = __ffma2_rn(f[0], lo2(x0), s0[b]);
+        s1[b] = __ffma2_rn(f[1], hi2(x0), s1[b]);
+        s0[b] = __ffma2_rn(f[2], lo2(x1), s0[b]);
+        s1[b] = __ffma2_rn(f[3], hi2(x1), s1[b]);
       }
     }
     const int g = g0 + gi;
     const float2 sbf = __half22float2(u32_as_h2(lds32(sb_row + 4 * g)));
-    const float s = sbf.x;
-    const float b8 = fmaf(8.f, s, sbf.y);
 #pragma unroll
     for (int b = 0; b < B; ++b)
-      acc[b] = fmaf(s, P[b], fmaf(b8, lds32f(xsum + b * xsum_b + 4 * g), acc[b]));
+      acc[b] = fmaf(sbf.x, (s0[b].x + s0[b].y) + (s1[b].x + s1[b].y),
+                    fmaf(sbf.y, lds32f(xsum + b * xsum_b + 4 * g), acc[b]));
   }
 }
 
@@ -695,8 +783,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   // call's grid completed) and the finisher count (each has a row group).
   const int tp_e = TP && crank == 0 ? tp_call_epoch(p.tp_own_flags) : 0;
   const int ld = L.kslice;  // staged row stride, in elements
-  if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
-  else if constexpr (F == kFmtQ8_0) stage_x_f32(p.x, xs, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
+  if constexpr (F == kFmtQ4_0) stage_x_q4_0(p.x, xs, xsum, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
+  else if constexpr (F == kFmtQ8_0) stage_x_q8_0(p.x, xs, xsum, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   else stage_x_affine<GS>(p.x, xs, xsum, p.nb, B, K, c0 * kChunkCols, cslice * kChunkCols, ld);
   __syncthreads();
 
@@ -743,11 +831,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
             const int cl = cl0 + j;
             const uint32_t src = slot + j * (32 * T::kChunkBytes);
             if constexpr (F == kFmtQ4_0) {
-              chunk_q4_0<B>(src, xs_a + cl * (kChunkCols * 2), xb, acc);
+              chunk_q4_0<B>(src, xs_a + cl * (kChunkCols * 4), xb, xsum_a + cl * 32, (ld / 32) * 4, acc);
             } else if constexpr (F == kFmtQ8_0) {
-              chunk_q8_0<B>(src, xs_a + cl * (kChunkCols * 4), xb, acc);
+              chunk_q8_0<B>(src, xs_a + cl * (kChunkCols * 4), xb, xsum_a + cl * 32, (ld / 32) * 4, acc);
             } else {
-              chunk_affine<B, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), xb, xsum_a,
+              chunk_affine<B, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 4), xb, xsum_a,
                                   (ld / GS) * 4, sb_a, cl * (kChunkCols / GS), acc);
             }
           }
@@ -764,7 +852,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     // Reduce the 4 warps, then the cs CTAs of the cluster.
     float* rd = red + (item & 1) * (kGemvWarps * B * 32);
 #pragma unroll
-    for (int b = 0; b < B; ++b) rd[(warp * B + b) * 32 + lane] = acc[b];
+    for (int b = 0; b < B; ++b) rd[(warp * B + b) * 32 + lane] = acc[b] * kUnscale;
     if (cs > 1 && item == 0) cluster_wait();  // every peer is running: DSMEM stores are safe
     __syncthreads();
     // Peers push their partial sums into the leader's slot buffer and arrive
@@ -808,7 +896,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     const int tp_nf = min(min(nclusters, p.num_rg), kTpFinishers);
     if (crank == 0 && cluster < tp_nf &&
         !tp_finish_cta(p.tp_own_buf, p.tp_own_flags, p.y, p.N, p.num_rg, p.tp_world, p.tp_rows, tp_e, cluster,
-                       tp_nf))
+                       tp_nf, p.tp_wait_ns))
       ok = false;
   }
   if (!ok) {

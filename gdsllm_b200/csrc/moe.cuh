@@ -35,7 +35,8 @@
 //     ring fed by 3-D TMA boxes whose z coordinate is the local expert index.
 //     Chunks of non-resident experts are never fetched.
 //   * Activations (x of the token, or h of the token's slots) are staged in
-//     shared memory in the dequantizer's pair order once per token.
+//     shared memory once per token, as scaled fp32 in the dequantizer's field
+//     order; products and sums are fp32 (gemv.cuh, "Exact fp32 products").
 #pragma once
 
 #include "gemv.cuh"
@@ -107,7 +108,7 @@ __host__ __device__ inline MoeSmemLayout moe_smem_layout(int C, int gs, int cs, 
   L.ring = off;
   off += kGemvWarps * stages * kMoeStageBytes;
   L.xs = off;
-  off += L.kslice * 2;
+  off += L.kslice * 4;  // scaled fp32 activations (gemv.cuh, stage_x_affine)
   L.xsum = off;
   const int gsl = L.kslice / gs;
   off += gsl * 4;
@@ -351,11 +352,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       if (ok) {
         const uint32_t src = ring_a + stage * kMoeStageBytes;
         if constexpr (STAGE == 0) {
-          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), 0, xsum_a, 0, sb_a,
+          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 4), 0, xsum_a, 0, sb_a,
                               cl * (kChunkCols / GS), acc);
         } else {
           float part[1] = {0.f};
-          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 2), 0, xsum_a, 0, sb_a,
+          chunk_affine<1, GS>(src, lane & 7, xs_a + cl * (kChunkCols * 4), 0, xsum_a, 0, sb_a,
                               cl * (kChunkCols / GS), part);
           acc[0] = fmaf(wt, part[0], acc[0]);
         }
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 
     // Reduce the 4 warps, then the cs CTAs of the cluster, into fin[0..31].
     float* rd = red + (done & 1) * (kGemvWarps * 32);
-    rd[warp * 32 + lane] = acc[0];
+    rd[warp * 32 + lane] = acc[0] * kUnscale;  // partial sums ran in units of 2^-39
     if (cs > 1 && !peers_waited) {
       cluster_wait();  // every peer is running: DSMEM stores are safe
       peers_waited = true;

@@ -42,6 +42,7 @@ struct P2PArgs {
   int cap;
   int rank;
   int world;
+  unsigned long long wait_ns;  // bound of the wait for the peers
 };
 
 __global__ void __launch_bounds__(kP2PThreads) allreduce_oneshot_kernel(const P2PArgs a) {
@@ -51,11 +52,15 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_oneshot_kernel(const P2
   const int lo = c * kP2PElemsPerCta;
   int* own = a.flags[a.rank] + c * kP2PMaxRanks;
   pdl_launch_dependents();  // the next kernel may prefetch its weights meanwhile
+  // The input is the previous kernel's output, and the epoch must be read
+  // only after the previous call of this kernel completed: a dependent
+  // launch can start while its predecessor still waits on the peers, and
+  // an epoch read then would reuse the predecessor's.
+  pdl_wait_primary();
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile int*>(own + a.rank) + 1;
     s_ok = 1;
   }
-  pdl_wait_primary();  // the input is the previous kernel's output
   __syncthreads();
   const int e = s_epoch;
   const size_t slot = (size_t)(e & 1) * a.cap;
@@ -73,7 +78,7 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_oneshot_kernel(const P2
     if (ld_acquire_sys(f) < e) {
       const unsigned long long t0 = global_timer_ns();
       while (ld_acquire_sys(f) < e) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > a.wait_ns) {
           record_device_error(kDevErrBarrierTimeout);
           s_ok = 0;
           break;
@@ -142,6 +147,7 @@ struct LLArgs {
   int cap;
   int rank;
   int world;
+  unsigned long long wait_ns;              // bound of the wait for the peers' words
 };
 
 template <typename T>
@@ -198,7 +204,7 @@ __global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const LLArgs a
       while (ok && (w[j] >> 32) != (unsigned long long)(unsigned)e) {
         if (t0 == 0) {
           t0 = global_timer_ns();
-        } else if (global_timer_ns() - t0 > kWaitLimitNs) {
+        } else if (global_timer_ns() - t0 > a.wait_ns) {
           record_device_error(kDevErrBarrierTimeout);
           ok = false;
           break;

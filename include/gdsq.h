@@ -70,6 +70,14 @@ GDSQ_API int gdsq_device_error(int device, int clear, int* out_bits);
  * writes weight memory. */
 GDSQ_API int gdsq_set_pdl(int enable);
 
+/* Upper bound, in nanoseconds, of every device-side wait for another GPU
+ * (gdsq_allreduce_sum_f16, gdsq_allreduce_sum_words and the finishers of
+ * gdsq_fused_gemv_allreduce) in launches made after the call; 0 restores
+ * the default of 1 s.  A wait that runs out sets device error bit 1 and the
+ * call returns without writing its output.  Returns the previous bound.  No
+ * reference counterpart (the reference runs one GPU). */
+GDSQ_API unsigned long long gdsq_set_peer_wait_limit_ns(unsigned long long ns);
+
 /* ---- Dequantization to fp16 ------------------------------------------- */
 
 /* Replaces launch_dequant_q4_0 (gdsllm/runtime/gguf_dequant.h:26-27).
@@ -177,7 +185,10 @@ GDSQ_API int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_s
  * streams (or host threads) at the same time overwrite each other's h, so
  * serialise them or use the two-call form with your own buffer.  The first
  * call on a device looks up the array's address (cudaGetSymbolAddress) and
- * must happen before any stream capture that records a later call. */
+ * must happen before any stream capture that records a later call; a first
+ * call on a capturing stream returns GDSQ_ERR_INVALID_VALUE.  The shared
+ * expert's nine tensors and shared_weights are all given or all null
+ * (GDSQ_ERR_INVALID_VALUE otherwise, before any CUDA call). */
 GDSQ_API int gdsq_moe_affine_q4_noalloc(const void* gate_weight, const void* gate_scales, const void* gate_biases,
                                         const void* up_weight, const void* up_scales, const void* up_biases,
                                         const void* down_weight, const void* down_scales, const void* down_biases,

@@ -23,7 +23,10 @@ BUILD = ORACLE / "_build"
 REF_OUT = ORACLE / "_ref"
 ORACLE_LIB = BUILD / "liboracle.so"
 REF_LIB = REF_OUT / "libref_kernels.so"
-REFERENCE_RUNTIME = Path(os.environ.get("GDSLLM_REFERENCE", "/root/reference")) / "gdsllm" / "runtime"
+# The reference checkout: $GDSLLM_REFERENCE, else a directory named
+# "reference" next to this repository.
+REFERENCE_ROOT = Path(os.environ.get("GDSLLM_REFERENCE", ORACLE.parent.parent / "reference"))
+REFERENCE_RUNTIME = REFERENCE_ROOT / "gdsllm" / "runtime"
 REF_SOURCES = ["fused_gemv.cu", "gguf_dequant.cu", "affine_q4_dequant.cu"]
 NVCC = str(Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "bin" / "nvcc")
 

@@ -140,4 +140,8 @@ def test_load_ops_read_files(ext, cuda, tmp_path):
     assert np.array_equal(t.cpu().numpy().view(np.uint8), data[4096:6144])
     with pytest.raises(RuntimeError):
         ext.load_file(str(path), data.size + 10)  # short read
+    with pytest.raises(RuntimeError, match="exceeds buffer size"):
+        ext.view_tensor(r, [4096], "float16", 0)  # 8192 bytes of a 4096-byte region
+    with pytest.raises(RuntimeError, match="exceeds buffer size"):
+        ext.view_tensor(r, [16], "int8", r.size - 8)
     ext.shutdown()

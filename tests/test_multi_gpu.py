@@ -135,6 +135,24 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             worst = max(worst, ((gout.float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
         del g
+        # back-to-back calls with programmatic dependent launch on, a GEMV
+        # (itself a dependent launch) between consecutive calls: each call's
+        # epoch must be read only after its predecessor completed
+        capi.set_pdl(True)
+        wq = synth.q4_0_weight(8192, 4096, seed=70).to(dev)
+        xs_in = [synth.activations(1, 4096, seed=71 + 3 * i + 97 * rank).to(dev) for i in range(12)]
+        ys = [torch.empty(1, 8192, dtype=torch.float16, device=dev) for _ in range(12)]
+        outs = [torch.empty(8192, dtype=torch.float16, device=dev) for _ in range(12)]
+        for rep in range(3):
+            for i in range(12):
+                capi.gemv_q4_0(wq, xs_in[i], 8192, 4096, out=ys[i])
+                ar(ys[i].view(-1), out=outs[i])
+            torch.cuda.synchronize()
+            for i in range(12):
+                ref = ys[i].view(-1).clone()
+                dist.all_reduce(ref)
+                worst = max(worst, ((outs[i].float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
+        capi.set_pdl(False)
         res["p2p"] = worst
         res["p2p_err"] = capi.device_error(rank, clear=True)
         torch.cuda.synchronize()

@@ -38,6 +38,18 @@ def test_noalloc_rejects_oversize_before_any_cuda_call():
     assert "static scratch" in msg and str(NOALLOC_MAX_H) in msg, msg
 
 
+@pytest.mark.parametrize("missing", [15, 16, 17, 21])
+def test_noalloc_rejects_partial_shared_expert(missing):
+    """Runs without a GPU: shared gate/up given but a shared down tensor or the
+    shared weights missing would make the two stages disagree on the slots
+    per token, so the call is rejected before any CUDA call."""
+    args = [16] * 23 + [1, 10, 4096, 1024, 128, 0, 512, 512, 0, None]
+    args[missing] = None  # 15-17: shared down weight/scales/biases, 21: shared_weights
+    st = lib().gdsq_moe_affine_q4_noalloc(*args)
+    assert st == 1  # GDSQ_ERR_INVALID_VALUE
+    assert "all given or all null" in lib().gdsq_last_error().decode()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("ntok,top_k,with_shared", [(1, 10, True), (8, 10, False), (3, 4, True)])
 def test_noalloc_matches_two_call_form(cuda, ntok, top_k, with_shared):
