@@ -17,13 +17,25 @@ dependent launch, replayed per token), timed with CUDA events, max over
 ranks.  ``e2e`` = the same tokens/s through the reference-facing op API
 (gds_io_ext.fused_dequant_gemv, called exactly as llama.py calls it) with
 the token's input copied host->device and the logits device->host every step.
+The same line also carries (unless --quick):
+  * ``e2e_decode``: config 1 as BASELINE states it -- 128 greedy tokens after
+    a 512-position prefill through GdsLLM's own CachedScheduler and
+    transformer_block, unchanged (attention, norms, RoPE, KV cache and the
+    full-table lm_head included), on this build's gds_io_ext (N = 1);
+    ``e2e_decode_scheduler_ops``: the same with gdsllm_b200.scheduler_ops'
+    embedding gather and fused lm_head installed;
+  * ``config0``: the 11008x4096 Q4_0 GEMV's GB/s and roofline;
+  * ``config3_tp``: the LLaMA-70B chain tensor-parallel over the N ranks;
+  * ``config4_ep``: the MoE decode expert-parallel over the N ranks, batch 1
+    and 8.
 
 --impl reference: the reference's path on this box: its CPU path (its dequant
 formula + torch.matmul on all host cores; the oracle port) as ``value``, and
 GdsLLM's own CUDA kernels, compiled unchanged for sm_100a, on the same token
-as ``ref_cuda``.
+as ``ref_cuda``, and through the same unchanged scheduler as ``e2e_decode``.
 
---gpus N (under torchrun): N independent replicas (weak scaling).
+--gpus N (under torchrun): N independent replicas of the default workload
+(weak scaling); config 3 and 4 in the same line run across the N ranks.
 --config 0: one 11008x4096 Q4_0 GEMV, rotating over copies larger than L2.
 --config 2: Q8_0 / affine-Q4 sweep (4 shapes x batch 1, 4, 8, 16).
 --config 3: LLaMA-70B-shaped decode chain, tensor-parallel over --gpus N (NCCL all-reduce).
@@ -383,6 +395,130 @@ def e2e_api(tok, ext, steps, warmup, dist):
 
 
 # ---------------------------------------------------------------------------
+# Config 1 as BASELINE states it: GdsLLM's own scheduler, unchanged
+
+REF_PACKAGE = ROOT / "baseline" / "_ref"
+DECODE_PREFILL, DECODE_WARMUP, DECODE_TOKENS = 512, 3, 128
+_MODEL_DIR = None
+
+
+def config1_model_dir(device) -> str:
+    """A LLaMA-7B-shaped model directory (config 1: 32 layers, Q4_0 body,
+    Q8_0 lm_head, fp16 embedding table, seeded weights) in the converter's
+    layout, written once per process under the system temporary directory
+    and removed at exit."""
+    global _MODEL_DIR
+    if _MODEL_DIR is None:
+        import atexit
+        import shutil
+        import tempfile
+        path = tempfile.mkdtemp(prefix="gdsllm_b200_config1_")
+        atexit.register(shutil.rmtree, path, True)
+        synth.write_llama_model_dir(path, layers=LAYERS, hidden=HIDDEN, heads=32, kv_heads=32, ffn=FFN, vocab=VOCAB,
+                                    max_seq_len=1024, body="q4_0", lm_head="q8_0", embed="f16", seed=0, device=device)
+        _MODEL_DIR = path
+    return _MODEL_DIR
+
+
+def e2e_decode(dist, module: str, scheduler_ops: bool = False):
+    """Greedy decode through GdsLLM's own CachedScheduler (the reference
+    package in baseline/_ref, unchanged): prompt of 509 tokens, 3 untimed
+    decode steps (KV prefilled to 512 positions), then 128 timed tokens, each
+    step a host token id in and the argmax token out (H2D + D2H per step), as
+    the reference's engine drives it.  ``module`` picks the gds_io_ext the
+    scheduler imports: "ours" (this build) or "reference" (GdsLLM's kernels
+    compiled unchanged, oracle/ref_module.py -- the reference arm only).
+    ``scheduler_ops`` also installs gdsllm_b200.scheduler_ops (embedding row
+    gather, fused lm_head) into the scheduler module."""
+    if not (REF_PACKAGE / "gdsllm" / "runtime" / "scheduler.py").exists():
+        return {"unavailable": "the reference package is not installed in baseline/_ref"}
+    if str(REF_PACKAGE) not in sys.path:
+        sys.path.insert(0, str(REF_PACKAGE))
+    import gdsllm_b200
+    from gdsllm.runtime import kv_cache, scheduler as sched_mod
+    if module == "ours":
+        gdsllm_b200.install_as_reference_module()
+    else:
+        from oracle import ref_module
+        ref_module.install()
+    saved = (sched_mod._embed_tokens, sched_mod._lm_head_proj)
+    if scheduler_ops:
+        from gdsllm_b200 import scheduler_ops as ops
+        ops.install(sched_mod)
+    path = config1_model_dir(dist.device)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, VOCAB, (1, DECODE_PREFILL - DECODE_WARMUP), generator=g)
+    tokens = []
+    try:
+        with torch.inference_mode(), sched_mod.CachedScheduler(path, device=str(dist.device)) as s:
+            c = s.config
+            kv = kv_cache.KVCache(c["num_layers"], c["num_kv_heads"], c["head_dim"], c["max_seq_len"],
+                                  device=dist.device)
+            logits = s.forward(prompt, kv_cache=kv, start_pos=0)
+            tok = int(logits[0, -1].argmax())
+            pos = prompt.shape[1]
+            for _ in range(DECODE_WARMUP):
+                logits = s.forward(torch.tensor([[tok]]), kv_cache=kv, start_pos=pos)
+                tok = int(logits[0, -1].argmax())
+                pos += 1
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            start.record()
+            for _ in range(DECODE_TOKENS):
+                logits = s.forward(torch.tensor([[tok]]), kv_cache=kv, start_pos=pos)
+                tok = int(logits[0, -1].argmax())  # D2H of the step's result
+                tokens.append(tok)
+                pos += 1
+            end.record()
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - t0
+            ms = start.elapsed_time(end)
+    finally:
+        sched_mod._embed_tokens, sched_mod._lm_head_proj = saved
+    return {"value": round(DECODE_TOKENS / (ms / 1e3), 2), "unit": "tok/s", "ms_per_token": round(ms / DECODE_TOKENS, 4),
+            "wall_s": round(wall, 3), "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+            "tokens_head": tokens[:8],
+            "what": ("GdsLLM's CachedScheduler + llama.transformer_block unchanged (baseline/_ref), config 1: 32 layers "
+                     "Q4_0, Q8_0 lm_head, fp16 embedding, KV prefilled to 512, 128 greedy tokens; gds_io_ext = "
+                     + ("this build" if module == "ours" else "GdsLLM's own kernels (oracle/ref_module.py)")
+                     + ("; embedding and lm_head through gdsllm_b200.scheduler_ops" if scheduler_ops else ""))}
+
+
+def _summary(res: dict, keys) -> dict:
+    return {k: res[k] for k in keys if k in res}
+
+
+def sub_benches(args, dist) -> dict:
+    """The other configurations' headline numbers for the default line (every
+    rank takes part, so at N > 1 the tensor- and expert-parallel exchanges
+    run): config 0's GB/s, config 3 (tensor parallel over the N ranks) and
+    config 4 (expert parallel over the N ranks, batch 1 and 8)."""
+    import argparse as _ap
+    out = {}
+
+    def sub(**kw):
+        a = _ap.Namespace(**vars(args))
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    r = bench_config0(sub(steps=max(20, min(args.steps, 100)), warmup=3), dist)
+    out["config0"] = _summary(r, ["metric", "value", "unit", "us_per_launch", "roofline", "clocks", "config"])
+    torch.cuda.empty_cache()
+    r = bench_config3(sub(steps=10, warmup=3), dist)
+    out["config3_tp"] = _summary(r, ["metric", "value", "unit", "ms_per_step", "scaling", "roofline",
+                                     "aggregate_weight_gbs", "clocks", "config"])
+    torch.cuda.empty_cache()
+    out["config4_ep"] = {}
+    for b in (1, 8):
+        r = bench_config4(sub(steps=10 if b == 1 else 5, warmup=3, batch=b, resident_layers=4), dist)
+        out["config4_ep"][f"batch{b}"] = _summary(r, ["value", "unit", "ms_per_step", "roofline", "clocks", "config"])
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # CPU path of the reference (dequant formula + torch.matmul), bounded sample
 
 def cpu_reference_path(budget_s: float = 0.0, max_items: int | None = None, frac: float = 1.0):
@@ -506,6 +642,13 @@ def bench_ours(args, dist):
         "gpu_launches": len(groups) * args.steps,
         "clocks": clock_info,
     }
+    if not args.quick:
+        if dist.world == 1:  # the scheduler loads onto one GPU
+            result["e2e_decode"] = e2e_decode(dist, "ours")
+            result["e2e_decode_scheduler_ops"] = e2e_decode(dist, "ours", scheduler_ops=True)
+        del tok
+        torch.cuda.empty_cache()
+        result.update(sub_benches(args, dist))
     return result
 
 
@@ -539,6 +682,9 @@ def bench_reference(args, dist):
         from oracle import reference_kernels as refk
         if refk.available():
             result["ref_cuda"] = bench_reference_cuda(args, dist, refk)
+            if dist.world == 1 and not args.quick:
+                # config 1 as BASELINE states it, on GdsLLM's own kernels
+                result["e2e_decode"] = e2e_decode(dist, "reference")
     except Exception as e:  # the CPU line above stands on its own
         result["ref_cuda"] = {"error": str(e)[:200]}
     return result
@@ -889,6 +1035,8 @@ def main():
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="default line only: skip the scheduler decode and the config 0 / 3 / 4 sub-benchmarks")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     dist = Dist(sample_clocks=args.impl != "reference")

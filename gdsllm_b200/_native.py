@@ -20,6 +20,8 @@ _C_SIGNATURES = {
     "gdsq_set_peer_wait_limit_ns": (ctypes.c_ulonglong, [ctypes.c_ulonglong]),
     "gdsq_dequant_q4_0": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
     "gdsq_dequant_q8_0": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
+    "gdsq_dequant_rows_gguf": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int,
+                                              ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_void_p]),
     "gdsq_dequant_affine_q4": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_void_p]),

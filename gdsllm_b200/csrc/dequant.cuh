@@ -88,6 +88,59 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Row gather: out[t][:] = the dequantized row ids[t] of a [rows][cols]
+// GGUF table (F: kFmtQ4_0 = 0 or kFmtQ8_0 = 1), the same bits as a full
+// dequantization followed by F.embedding, which the reference's callers do
+// for the embedding (gdsllm/runtime/scheduler.py:22-45).  Unit u covers 8
+// outputs of token u / (4 * blocks_per_row), in the order of the kernels
+// above.  An id outside 0..rows-1 sets device error bit 4 and yields zeros.
+template <int F, bool kVecStore>
+__global__ void __launch_bounds__(256)
+    dequant_rows_kernel(const uint8_t* __restrict__ src, const long long* __restrict__ ids, long long rows,
+                        int blocks_per_row, __half* __restrict__ dst, uint64_t units) {
+  constexpr int kBlockBytes = F == 0 ? 18 : 34;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const uint64_t per_token = (uint64_t)blocks_per_row * 4;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += stride) {
+    const uint64_t tok = u / per_token;
+    const uint64_t r = u - tok * per_token;
+    const long long id = __ldg(ids + tok);
+    float v[8];
+    if (id < 0 || id >= rows) {
+      if (r == 0) record_device_error(kDevErrBadIndex);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+    } else {
+      const uint64_t blk = (uint64_t)id * blocks_per_row + (r >> 2);
+      const int t = static_cast<int>(r & 3);
+      const uint16_t* bp = reinterpret_cast<const uint16_t*>(src + blk * kBlockBytes);
+      const float d = __half2float(__ushort_as_half(__ldg(bp)));
+      if constexpr (F == 0) {
+        const uint16_t* qp = bp + 1 + 4 * (t & 1);
+        const uint32_t lo = (uint32_t)__ldg(qp) | ((uint32_t)__ldg(qp + 1) << 16);
+        const uint32_t hi = (uint32_t)__ldg(qp + 2) | ((uint32_t)__ldg(qp + 3) << 16);
+        const int sh = (t >> 1) * 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[k] = d * float((int)((lo >> (8 * k + sh)) & 15u) - 8);
+          v[k + 4] = d * float((int)((hi >> (8 * k + sh)) & 15u) - 8);
+        }
+      } else {
+        const uint16_t* qp = bp + 1 + 4 * t;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t two = __ldg(qp + k);
+          v[2 * k] = d * float(static_cast<int8_t>(two & 0xFFu));
+          v[2 * k + 1] = d * float(static_cast<int8_t>(two >> 8));
+        }
+      }
+    }
+    store8<kVecStore>(dst + u * 8, v);
+  }
+}
+
 // Unit u = packed word u (8 nibbles, LSB first) -> outputs [8u, 8u+8).
 template <bool kVecStore>
 __global__ void __launch_bounds__(256)

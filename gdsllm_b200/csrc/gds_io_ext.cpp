@@ -404,6 +404,38 @@ torch::Tensor py_dequant_gguf(Handle h, std::vector<int64_t> shape, const std::s
   return out;
 }
 
+// Additive: F.embedding over a GGUF table without dequantizing the whole
+// table (the reference's _embed_tokens does, gdsllm/runtime/scheduler.py:
+// 22-45).  token_ids: int64 CUDA tensor of any shape; returns fp16
+// [*token_ids.shape, cols], bit-identical to dequant_gguf + F.embedding.
+torch::Tensor py_embedding_gguf(Handle h, torch::Tensor token_ids, std::vector<int64_t> shape,
+                                const std::string& gguf_type, int64_t offset) {
+  const char* op = "py_embedding_gguf";
+  require_handle(h, op);
+  if (shape.size() != 2) throw std::runtime_error("py_embedding_gguf: shape must be [rows, cols]");
+  const int64_t rows = shape[0], cols = shape[1];
+  if (cols % 32 != 0)
+    throw std::runtime_error("py_embedding_gguf: cols must be a multiple of 32, got " + std::to_string(cols));
+  int64_t block_bytes;
+  if (gguf_type == "q4_0") block_bytes = 18;
+  else if (gguf_type == "q8_0") block_bytes = 34;
+  else throw std::runtime_error("py_embedding_gguf: unsupported type '" + gguf_type + "'");
+  if (!token_ids.is_cuda() || token_ids.get_device() != h->device_id() || token_ids.scalar_type() != torch::kLong)
+    throw std::runtime_error("py_embedding_gguf: token_ids must be an int64 tensor on the buffer's device");
+  require_range(h, offset, rows * (cols / 32) * block_bytes, op, "table bytes");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(h->device_id()));
+  torch::Tensor ids = token_ids.contiguous();
+  std::vector<int64_t> out_shape(ids.sizes().begin(), ids.sizes().end());
+  out_shape.push_back(cols);
+  auto opts = torch::TensorOptions().dtype(torch::kFloat16).device(torch::kCUDA, h->device_id());
+  torch::Tensor out = torch::empty(out_shape, opts);
+  const int st = gdsq_dequant_rows_gguf(gguf_type == "q4_0" ? GDSQ_TYPE_Q4_0 : GDSQ_TYPE_Q8_0, at_offset(h, offset),
+                                        rows, static_cast<int>(cols), reinterpret_cast<const long long*>(ids.data_ptr()),
+                                        ids.numel(), out.data_ptr(), current_stream(h));
+  raise_status(st, op);
+  return out;
+}
+
 // gdsllm/runtime/gds_bindings.cpp:333-387
 torch::Tensor py_fused_dequant_gemv(Handle h, torch::Tensor x, std::vector<int64_t> weight_shape,
                                     const std::string& gguf_type, int64_t offset) {
@@ -710,6 +742,9 @@ PYBIND11_MODULE(gds_io_ext, m) {
         py::arg("output") = py::none());
   m.def("fused_dequant_gemv", &py_fused_dequant_gemv, "Fused dequant + GEMV for Q4_0/Q8_0 (decode).",
         py::arg("handle"), py::arg("x"), py::arg("weight_shape"), py::arg("gguf_type"), py::arg("offset"));
+  m.def("embedding_gguf", &py_embedding_gguf,
+        "Embedding lookup over a GGUF Q4_0/Q8_0 table: dequantizes only the looked-up rows.", py::arg("handle"),
+        py::arg("token_ids"), py::arg("shape"), py::arg("gguf_type"), py::arg("offset"));
   m.def("dequant_affine_q4", &py_dequant_affine_q4, "Dequantize affine Q4 (uint32 + scales + biases) to fp16.",
         py::arg("handle"), py::arg("weight_shape"), py::arg("weight_offset"), py::arg("scale_offset"),
         py::arg("bias_offset"), py::arg("group_size"), py::arg("output") = py::none());

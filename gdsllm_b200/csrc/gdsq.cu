@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -786,13 +787,20 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
   auto kernel = moe_affine_kernel<STAGE, GS>;
   int force_cs = 0, force_st = 0;
   bool forced = false;
-  if (const char* e = getenv("GDSQ_MOE_PLAN")) {
+  // Tuning sweeps: "cs:stages" for both stages (GDSQ_MOE_PLAN) or one
+  // (GDSQ_MOE_PLAN0 / GDSQ_MOE_PLAN1).
+  const char* e_stage = getenv(STAGE == 0 ? "GDSQ_MOE_PLAN0" : "GDSQ_MOE_PLAN1");
+  if (const char* e = e_stage ? e_stage : getenv("GDSQ_MOE_PLAN")) {
     forced = sscanf(e, "%d:%d", &force_cs, &force_st) == 2 && force_cs >= 1 && force_cs <= kMaxCluster &&
              force_st >= 1 && force_st <= kMaxStages;
   }
   double best = 1e30;
   bool found = false;
-  for (int cs = 1; cs <= kMaxCluster; cs *= 2) {
+  // Gate/up (K = hidden, 16 + 16 rows per item, many items): measured on
+  // B200 over the config-4 decode step, splits above 2 lose (B = 1: 306
+  // tok/s at cs = 2 vs 267 at cs = 4), so the model chooses among 1 and 2.
+  const int max_cs = STAGE == 0 ? 2 : kMaxCluster;
+  for (int cs = 1; cs <= max_cs || (forced && cs <= kMaxCluster); cs *= 2) {
     if (cs > C) break;
     if (forced && cs != force_cs) continue;
     const int cslice = (C + cs - 1) / cs;
@@ -1130,6 +1138,40 @@ int gdsq_dequant_q8_0(const void* src, void* dst, uint64_t num_blocks, void* str
                       ? launch(dequant_q8_0_kernel<true>, dim3(grid), dim3(256), 0, stream, false, s, d, units)
                       : launch(dequant_q8_0_kernel<false>, dim3(grid), dim3(256), 0, stream, false, s, d, units);
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "dequant q8_0 launch");
+}
+
+int gdsq_dequant_rows_gguf(int gguf_type, const void* table, long long rows, int cols, const long long* ids,
+                           long long num_ids, void* dst, void* stream_v) {
+  t_last_error.clear();
+  if (gguf_type != GDSQ_TYPE_Q4_0 && gguf_type != GDSQ_TYPE_Q8_0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "dequant rows: gguf_type %d is neither Q4_0 nor Q8_0", gguf_type);
+  if (rows < 0 || cols < 0 || cols % 32 != 0 || num_ids < 0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "dequant rows: table [%lld, %d] (cols must be a multiple of 32), %lld ids",
+                rows, cols, num_ids);
+  if (num_ids == 0 || cols == 0) return GDSQ_OK;
+  if (!table || !ids || !dst) return fail(GDSQ_ERR_INVALID_VALUE, "dequant rows: null pointer");
+  if (!aligned(table, 2) || !aligned(dst, 2) || !aligned(ids, 8))
+    return fail(GDSQ_ERR_MISALIGNED, "dequant rows: table/output must be 2-byte and ids 8-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  const uint64_t units = (uint64_t)num_ids * (cols / 32) * 4;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const unsigned grid = dequant_grid(units, *dev);
+  const uint8_t* s = static_cast<const uint8_t*>(table);
+  __half* d = static_cast<__half*>(dst);
+  const int bpr = cols / 32;
+  const bool vec = aligned(dst, 16);
+  cudaError_t e;
+  if (gguf_type == GDSQ_TYPE_Q4_0)
+    e = vec ? launch(dequant_rows_kernel<0, true>, dim3(grid), dim3(256), 0, stream, false, s, ids, rows, bpr, d, units)
+            : launch(dequant_rows_kernel<0, false>, dim3(grid), dim3(256), 0, stream, false, s, ids, rows, bpr, d,
+                     units);
+  else
+    e = vec ? launch(dequant_rows_kernel<1, true>, dim3(grid), dim3(256), 0, stream, false, s, ids, rows, bpr, d, units)
+            : launch(dequant_rows_kernel<1, false>, dim3(grid), dim3(256), 0, stream, false, s, ids, rows, bpr, d,
+                     units);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "dequant rows launch");
 }
 
 int gdsq_dequant_affine_q4(const void* weight, const void* scales, const void* biases, void* dst,

@@ -523,6 +523,77 @@ __global__ void __launch_bounds__(256) moe_down_generic_kernel(const MoeParams p
 // topk / sort / softmax / cast / linear / sigmoid chain of small torch
 // kernels (and their host-visible ids) with one launch.
 constexpr int kRouteMaxExperts = 4096;
+constexpr int kRouteLaneVals = 16;  // fast selection: up to 32 x 16 = 512 experts, top-k <= 32
+
+// (v, i) ranks before (w, j): the larger logit first, equal logits by the
+// lower expert index.
+__device__ __forceinline__ bool route_before(float v, int i, float w, int j) {
+  return v > w || (v == w && i < j);
+}
+
+// Top-k by one warp for E <= 512, K <= 32: every lane sorts its (at most 16)
+// strided logits in registers (a bitonic network, no memory traffic), then k
+// rounds take the best lane head by a warp arg-max and the winning lane
+// pops its head.  Lane r returns the r-th selection.
+__device__ __forceinline__ void route_select_sorted(const __half* __restrict__ lg, int E, int K, int lane,
+                                                    float* sel_v, int* sel_i) {
+  float v[kRouteLaneVals];
+  int ix[kRouteLaneVals];
+#pragma unroll
+  for (int j = 0; j < kRouteLaneVals; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = i < E ? __half2float(lg[i]) : -INFINITY;
+    ix[j] = i < E ? i : 0x7fffffff;
+  }
+#pragma unroll
+  for (int k = 2; k <= kRouteLaneVals; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < kRouteLaneVals; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const bool first = (i & k) == 0;  // this pair's order: i before l, else l before i
+          const bool swap = first ? route_before(v[l], ix[l], v[i], ix[i]) : route_before(v[i], ix[i], v[l], ix[l]);
+          if (swap) {
+            const float tv = v[i];
+            v[i] = v[l];
+            v[l] = tv;
+            const int ti = ix[i];
+            ix[i] = ix[l];
+            ix[l] = ti;
+          }
+        }
+      }
+    }
+  }
+  for (int r = 0; r < K; ++r) {
+    float bv = v[0];
+    int bi = ix[0];
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+      if (route_before(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (r == lane) {
+      *sel_v = bv;
+      *sel_i = bi;
+    }
+    if (ix[0] == bi) {  // this lane's head was taken (expert indices are unique)
+#pragma unroll
+      for (int j = 0; j + 1 < kRouteLaneVals; ++j) {
+        v[j] = v[j + 1];
+        ix[j] = ix[j + 1];
+      }
+      v[kRouteLaneVals - 1] = -INFINITY;
+      ix[kRouteLaneVals - 1] = 0x7fffffff;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict__ logits, int E, int K,
                                                        const __half* __restrict__ x,
@@ -535,6 +606,11 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
   pdl_launch_dependents();
   pdl_wait_primary();
   if (warp == 0) {
+    float sel_v = 0.f;  // lane r keeps the r-th selected logit
+    int sel_i = 0;
+    if (E <= 32 * kRouteLaneVals && K <= 32) {
+      route_select_sorted(logits + (size_t)tok * E, E, K, lane, &sel_v, &sel_i);
+    } else {
     for (int i = lane; i < E; i += 32) vals[i] = __half2float(logits[(size_t)tok * E + i]);
     __syncwarp();
     // Each lane tracks the best of its own strided elements.
@@ -552,8 +628,6 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
     float bv;
     int bi;
     lane_best(&bv, &bi);
-    float sel_v = 0.f;  // lane r keeps the r-th selected logit
-    int sel_i = 0;
     for (int r = 0; r < K; ++r) {
       float v = bv;
       int i = bi;
@@ -580,6 +654,7 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
         vals[E + lane] = sel_v;  // park the value for the softmax
       }
     }
+    }
     // softmax over the K selected logits (the first is the largest)
     __syncwarp();
     if (K > 32) {
@@ -603,6 +678,7 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
   } else if (g != nullptr) {
     float acc = 0.f;
     const __half* xr = x + (size_t)tok * H;
+#pragma unroll 8  // independent 16-byte loads in flight, not one round trip per step
     for (int j = lane * 8; j < H; j += 32 * 8) {
       const uint4 xv = *reinterpret_cast<const uint4*>(xr + j);
       const uint4 gv = *reinterpret_cast<const uint4*>(g + j);

@@ -88,6 +88,16 @@ GDSQ_API int gdsq_dequant_q4_0(const void* src, void* dst, uint64_t num_blocks, 
  * src: num_blocks * 34 bytes (2-byte aligned); dst: num_blocks * 32 fp16. */
 GDSQ_API int gdsq_dequant_q8_0(const void* src, void* dst, uint64_t num_blocks, void* stream);
 
+/* dst[t][:] = the fp16 dequantization of row ids[t] of a GGUF Q4_0 / Q8_0
+ * table [rows][cols] (gguf_type GDSQ_TYPE_Q4_0 / GDSQ_TYPE_Q8_0), the same
+ * bits as dequantizing the whole table and gathering the rows.  Replaces the
+ * embedding lookup of the reference's callers, which dequantize the full
+ * table per call (gdsllm/runtime/scheduler.py:22-45, no single launcher).
+ * ids: num_ids int64 on the device (8-byte aligned); dst: num_ids * cols fp16.
+ * An id outside 0..rows-1 gives a zero row and sets device error bit 4. */
+GDSQ_API int gdsq_dequant_rows_gguf(int gguf_type, const void* table, long long rows, int cols,
+                                    const long long* ids, long long num_ids, void* dst, void* stream);
+
 /* Replaces launch_dequant_affine_q4 (gdsllm/runtime/affine_q4_dequant.h:29-32).
  * weight: num_elements/8 uint32 (4-byte aligned); scales, biases:
  * num_elements/group_size fp16; dst: num_elements fp16.  in_dim must be a

@@ -67,7 +67,35 @@ def build_reference_kernels(force: bool = False) -> Path | None:
     return REF_LIB
 
 
+REF_PACKAGE = ORACLE.parent / "baseline" / "_ref"
+
+
+def install_reference_package(force: bool = False) -> Path | None:
+    """Installs the reference package (its Python modules and its compiled
+    extension) into baseline/_ref, the one offline pip install this project
+    makes, so that tests can run the reference's own callers (llama.py,
+    scheduler.py, qwen_moe.py).  The build writes into its source tree, so it
+    runs on a copy under the system temporary directory.  Returns the target,
+    or None when the reference tree is absent."""
+    import shutil
+    import tempfile
+
+    if (REF_PACKAGE / "gdsllm" / "runtime" / "scheduler.py").exists() and not force:
+        return REF_PACKAGE
+    if not REFERENCE_RUNTIME.is_dir():
+        return None
+    with tempfile.TemporaryDirectory() as tmp:
+        src = Path(tmp) / "reference"
+        shutil.copytree(REFERENCE_ROOT, src)
+        env = dict(os.environ, TORCH_CUDA_ARCH_LIST="10.0a")
+        subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                        "--find-links", "/opt/wheelhouse", "--upgrade", "--target", str(REF_PACKAGE), str(src)],
+                       check=True, env=env)
+    return REF_PACKAGE
+
+
 if __name__ == "__main__":
     force = "--force" in sys.argv
     print(build_oracle(force))
     print(build_reference_kernels(force))
+    print(install_reference_package(force))

@@ -318,7 +318,8 @@ def test_moe_clamp_flag(gdsq, cuda):
     assert torch.isfinite(y_cl).all() and y_cl.abs().max().item() == 65504.0
 
 
-@pytest.mark.parametrize("ntok,experts,top_k", [(1, 512, 10), (8, 512, 10), (5, 64, 7), (2, 128, 40)])
+@pytest.mark.parametrize("ntok,experts,top_k", [(1, 512, 10), (8, 512, 10), (5, 64, 7), (4, 512, 32), (3, 33, 1),
+                                                (2, 128, 40), (3, 1000, 12)])
 def test_moe_route_kernel_matches_torch_topk(gdsq, cuda, ntok, experts, top_k):
     """Top-k set exactly as torch.topk on the same fp16 logits (ties at the
     boundary excepted, there any equal logit is a valid pick), softmax weights
