@@ -107,6 +107,10 @@ class Dist:
         if self.world > 1:
             import datetime
             import torch.distributed as dist
+            # Rank 0's stdout carries exactly one JSON line: keep NCCL's
+            # version banner (printed at NCCL_DEBUG=VERSION) off it.
+            if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+                os.environ["NCCL_DEBUG"] = "WARN"
             dist.init_process_group("nccl", device_id=self.device,
                                     timeout=datetime.timedelta(seconds=120))
 

@@ -30,13 +30,16 @@
 
 #include <algorithm>
 #include <cerrno>
+#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <tuple>
+#include <unordered_map>
 #include <vector>
 
 #include "gdsq.h"
@@ -242,6 +245,189 @@ ssize_t gds_read(GdsBufferHandle& buf, const std::string& path, size_t size, off
   return static_cast<ssize_t>(done);
 }
 
+// ---------------------------------------------------------------------------
+// Asynchronous, double-buffered loading (additive).  The reference reads a
+// layer synchronously before its compute (gdsllm/runtime/gds_io.cu:135-191,
+// called from torch_bridge.py:148-177), so the GPU idles while a layer that
+// is not resident is read.  load_file_async() returns at once with a
+// PendingLoad.  One worker thread per process reads the file in chunks into
+// two pinned staging buffers in turn and copies each chunk to the device
+// with one cudaMemcpyAsync on its own stream: the read of chunk i + 1
+// overlaps the copy of chunk i, and both overlap whatever the caller's
+// streams run meanwhile.  PendingLoad.wait() returns the buffer handle once
+// the reads are done and makes the caller's current stream wait, on the
+// device, for the copies, so work queued after it sees the data.
+
+constexpr size_t kAsyncChunk = size_t(8) << 20;
+
+struct LoadJob {
+  Handle h;
+  std::string path;
+  size_t size = 0;
+  off_t file_offset = 0;
+  std::mutex m;
+  std::condition_variable cv;
+  bool done = false;
+  std::string error;
+  cudaEvent_t copied = nullptr;  // recorded on the loader's stream after the last copy
+  ~LoadJob() {
+    if (copied) cudaEventDestroy(copied);  // a load nobody waited for
+  }
+};
+
+class AsyncLoader {
+ public:
+  static AsyncLoader& get() {
+    static AsyncLoader* loader = new AsyncLoader();  // never destroyed: the worker runs until exit
+    return *loader;
+  }
+
+  std::shared_ptr<LoadJob> submit(Handle h, const std::string& path, size_t size, off_t file_offset) {
+    auto job = std::make_shared<LoadJob>();
+    job->h = std::move(h);
+    job->path = path;
+    job->size = size;
+    job->file_offset = file_offset;
+    {
+      std::lock_guard<std::mutex> lock(m_);
+      queue_.push_back(job);
+    }
+    cv_.notify_one();
+    return job;
+  }
+
+ private:
+  AsyncLoader() { std::thread([this] { loop(); }).detach(); }
+
+  void loop() {
+    for (;;) {
+      std::shared_ptr<LoadJob> job;
+      {
+        std::unique_lock<std::mutex> lock(m_);
+        cv_.wait(lock, [this] { return !queue_.empty(); });
+        job = queue_.front();
+        queue_.erase(queue_.begin());
+      }
+      std::string err;
+      try {
+        run(*job);
+      } catch (const std::exception& ex) {
+        err = ex.what();
+      }
+      {
+        std::lock_guard<std::mutex> lock(job->m);
+        job->error = err;
+        job->done = true;
+      }
+      job->cv.notify_all();
+    }
+  }
+
+  // Per device: the copy stream and the two pinned staging buffers, each
+  // with an event recorded after the copy that last read it.
+  struct DeviceState {
+    cudaStream_t stream = nullptr;
+    void* staging[2] = {nullptr, nullptr};
+    cudaEvent_t free[2] = {nullptr, nullptr};
+  };
+
+  DeviceState& state(int dev) {
+    DeviceState& d = devices_[dev];
+    if (!d.stream) {
+      check_cuda(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking), "load_file_async: stream");
+      for (int i = 0; i < 2; ++i) {
+        check_cuda(cudaHostAlloc(&d.staging[i], kAsyncChunk, cudaHostAllocPortable), "load_file_async: cudaHostAlloc");
+        check_cuda(cudaEventCreateWithFlags(&d.free[i], cudaEventDisableTiming | cudaEventBlockingSync),
+                   "load_file_async: cudaEventCreate");
+        check_cuda(cudaEventRecord(d.free[i], d.stream), "load_file_async: cudaEventRecord");
+      }
+    }
+    return d;
+  }
+
+  void run(LoadJob& job) {
+    const int dev = job.h->device_id();
+    check_cuda(cudaSetDevice(dev), "load_file_async: cudaSetDevice");
+    DeviceState& d = state(dev);
+    int fd = open(job.path.c_str(), O_RDONLY);
+    if (fd < 0) throw std::runtime_error("load_file_async: cannot open file '" + job.path + "': " + strerror(errno));
+    size_t done = 0;
+    int b = 0;
+    cudaError_t e = cudaSuccess;
+    while (done < job.size) {
+      // the copy that last read this staging buffer must be finished
+      e = cudaEventSynchronize(d.free[b]);
+      if (e != cudaSuccess) break;
+      const size_t want = std::min(kAsyncChunk, job.size - done);
+      const ssize_t n = pread(fd, d.staging[b], want, job.file_offset + static_cast<off_t>(done));
+      if (n <= 0) break;
+      e = cudaMemcpyAsync(static_cast<char*>(job.h->dev_ptr()) + done, d.staging[b], static_cast<size_t>(n),
+                          cudaMemcpyHostToDevice, d.stream);
+      if (e == cudaSuccess) e = cudaEventRecord(d.free[b], d.stream);
+      if (e != cudaSuccess) break;
+      done += static_cast<size_t>(n);
+      b ^= 1;
+    }
+    close(fd);
+    if (e != cudaSuccess || done < job.size) cudaStreamSynchronize(d.stream);  // no copy outlives a failed load
+    check_cuda(e, "load_file_async: copy");
+    if (done < job.size)
+      throw std::runtime_error("load_file_async: expected " + std::to_string(job.size) + " bytes, got " +
+                               std::to_string(done));
+    check_cuda(cudaEventCreateWithFlags(&job.copied, cudaEventDisableTiming), "load_file_async: cudaEventCreate");
+    check_cuda(cudaEventRecord(job.copied, d.stream), "load_file_async: cudaEventRecord");
+  }
+
+  std::mutex m_;
+  std::condition_variable cv_;
+  std::vector<std::shared_ptr<LoadJob>> queue_;
+  std::unordered_map<int, DeviceState> devices_;  // touched by the worker thread only
+};
+
+// The Python-side handle of one asynchronous load.
+class PendingLoad {
+ public:
+  explicit PendingLoad(std::shared_ptr<LoadJob> job) : job_(std::move(job)) {}
+
+  bool ready() {
+    std::lock_guard<std::mutex> lock(job_->m);
+    return job_->done;
+  }
+
+  // Blocks (without the GIL) until the file is read, then orders the copies
+  // before later work on the current stream of the buffer's device.
+  Handle wait() {
+    {
+      py::gil_scoped_release release;
+      std::unique_lock<std::mutex> lock(job_->m);
+      job_->cv.wait(lock, [this] { return job_->done; });
+    }
+    if (!job_->error.empty()) throw std::runtime_error(job_->error);
+    if (job_->copied) {
+      const int dev = job_->h->device_id();
+      c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(dev));
+      cudaStream_t s = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(dev)).stream();
+      check_cuda(cudaStreamWaitEvent(s, job_->copied, 0), "PendingLoad.wait: cudaStreamWaitEvent");
+      cudaEventDestroy(job_->copied);
+      job_->copied = nullptr;
+    }
+    return job_->h;
+  }
+
+ private:
+  std::shared_ptr<LoadJob> job_;
+};
+
+// load_file / load_file_region without blocking: the buffer is allocated
+// now (on device_id), the read and the copies run on the loader's thread.
+PendingLoad py_load_file_async(const std::string& filepath, int64_t size_bytes, int64_t file_offset, int device_id) {
+  if (size_bytes < 0 || file_offset < 0)
+    throw std::runtime_error("load_file_async: negative size or offset");
+  auto h = GdsBufferHandle::allocate(static_cast<size_t>(size_bytes), device_id);
+  return PendingLoad(AsyncLoader::get().submit(h, filepath, static_cast<size_t>(size_bytes),
+                                               static_cast<off_t>(file_offset)));
+}
+
 torch::Dtype parse_dtype(const std::string& s) {
   if (s == "float16" || s == "half") return torch::kFloat16;
   if (s == "float32" || s == "float") return torch::kFloat32;
@@ -313,7 +499,43 @@ void* current_stream(const Handle& h) {
 // ---------------------------------------------------------------------------
 // Load / view ops (gdsllm/runtime/gds_bindings.cpp:95-247)
 
+// Prefetches started with prefetch_file(), picked up by the next load_file /
+// load_file_region of the same (path, size, offset, device): a caller that
+// prefetches layer i + 1 before computing layer i gets the read and the
+// copies overlapped with that compute, and the reference's unchanged
+// ModelWeights.load_layer (gdsllm/runtime/torch_bridge.py:148-177) receives
+// the prefetched buffer.
+using PrefetchKey = std::tuple<std::string, int64_t, int64_t, int>;
+struct PrefetchKeyHash {
+  size_t operator()(const PrefetchKey& k) const {
+    return std::hash<std::string>()(std::get<0>(k)) ^ (std::hash<int64_t>()(std::get<1>(k)) * 31) ^
+           (std::hash<int64_t>()(std::get<2>(k)) * 131) ^ std::hash<int>()(std::get<3>(k));
+  }
+};
+std::mutex g_prefetch_mutex;
+std::unordered_map<PrefetchKey, std::shared_ptr<PendingLoad>, PrefetchKeyHash> g_prefetched;
+
+void py_prefetch_file(const std::string& path, int64_t size_bytes, int64_t file_offset, int device_id) {
+  auto pending = std::make_shared<PendingLoad>(py_load_file_async(path, size_bytes, file_offset, device_id));
+  std::lock_guard<std::mutex> lock(g_prefetch_mutex);
+  g_prefetched[PrefetchKey(path, size_bytes, file_offset, device_id)] = std::move(pending);
+}
+
+// The prefetched buffer of this exact region, if any (waited for), else null.
+Handle take_prefetched(const std::string& path, int64_t size_bytes, int64_t file_offset, int device_id) {
+  std::shared_ptr<PendingLoad> pending;
+  {
+    std::lock_guard<std::mutex> lock(g_prefetch_mutex);
+    auto it = g_prefetched.find(PrefetchKey(path, size_bytes, file_offset, device_id));
+    if (it == g_prefetched.end()) return nullptr;
+    pending = it->second;
+    g_prefetched.erase(it);
+  }
+  return pending->wait();
+}
+
 Handle py_load_file(const std::string& path, int64_t size_bytes, int device_id) {
+  if (Handle pre = take_prefetched(path, size_bytes, 0, device_id)) return pre;
   auto h = GdsBufferHandle::allocate(size_bytes, device_id);
   ssize_t n = gds_read(*h, path, size_bytes, 0, 0);
   if (n < size_bytes)
@@ -324,6 +546,7 @@ Handle py_load_file(const std::string& path, int64_t size_bytes, int device_id) 
 
 Handle py_load_file_region(const std::string& path, int64_t size_bytes, int64_t file_offset,
                            int device_id) {
+  if (Handle pre = take_prefetched(path, size_bytes, file_offset, device_id)) return pre;
   auto h = GdsBufferHandle::allocate(size_bytes, device_id);
   ssize_t n = gds_read(*h, path, size_bytes, file_offset, 0);
   if (n < size_bytes)
@@ -742,6 +965,18 @@ PYBIND11_MODULE(gds_io_ext, m) {
         py::arg("output") = py::none());
   m.def("fused_dequant_gemv", &py_fused_dequant_gemv, "Fused dequant + GEMV for Q4_0/Q8_0 (decode).",
         py::arg("handle"), py::arg("x"), py::arg("weight_shape"), py::arg("gguf_type"), py::arg("offset"));
+  py::class_<PendingLoad>(m, "PendingLoad", "An asynchronous file load started by load_file_async.")
+      .def_property_readonly("ready", &PendingLoad::ready, "True once the file has been read.")
+      .def("wait", &PendingLoad::wait,
+           "Waits for the read, orders the copies before later work on the current stream and returns the "
+           "GdsBufferHandle.");
+  m.def("load_file_async", &py_load_file_async,
+        "Start loading a file region into a new CUDA buffer without blocking: double-buffered pinned staging, "
+        "one cudaMemcpyAsync per chunk on a loader stream.",
+        py::arg("filepath"), py::arg("size_bytes"), py::arg("file_offset") = 0, py::arg("device_id") = 0);
+  m.def("prefetch_file", &py_prefetch_file,
+        "load_file_async whose buffer the next load_file / load_file_region of the same region returns.",
+        py::arg("filepath"), py::arg("size_bytes"), py::arg("file_offset") = 0, py::arg("device_id") = 0);
   m.def("embedding_gguf", &py_embedding_gguf,
         "Embedding lookup over a GGUF Q4_0/Q8_0 table: dequantizes only the looked-up rows.", py::arg("handle"),
         py::arg("token_ids"), py::arg("shape"), py::arg("gguf_type"), py::arg("offset"));

@@ -145,3 +145,40 @@ def test_load_ops_read_files(ext, cuda, tmp_path):
     with pytest.raises(RuntimeError, match="exceeds buffer size"):
         ext.view_tensor(r, [16], "int8", r.size - 8)
     ext.shutdown()
+
+
+def test_load_file_async_and_prefetch(ext, cuda, tmp_path):
+    """load_file_async reads through two pinned staging buffers with one
+    cudaMemcpyAsync per chunk on a loader stream while the caller's stream
+    keeps running; wait() returns the same bytes load_file reads.  A
+    prefetch_file()d region is what the next load_file / load_file_region of
+    that region returns."""
+    from gdsllm_b200 import capi, synth
+    rng = np.random.default_rng(1)
+    data = rng.integers(0, 256, (40 << 20) + 123, dtype=np.uint8)  # 5+ chunks, ragged tail
+    path = tmp_path / "layer_007.bin"
+    data.tofile(path)
+    ext.init()
+    pending = [ext.load_file_async(str(path), data.size),
+               ext.load_file_async(str(path), 10_000_000, 12345),
+               ext.load_file_async(str(path), 4096, data.size - 4096)]
+    w = synth.q4_0_weight(4096, 4096, seed=1).to(cuda)   # the caller's stream stays busy meanwhile
+    x = synth.activations(1, 4096, seed=2).to(cuda)
+    for _ in range(20):
+        capi.gemv_q4_0(w, x, 4096, 4096)
+    handles = [p.wait() for p in reversed(pending)][::-1]
+    assert all(p.ready for p in pending)
+    got = [ext.view_tensor(h, [n], "int8", 0).cpu().numpy().view(np.uint8)
+           for h, n in zip(handles, [data.size, 10_000_000, 4096])]
+    assert np.array_equal(got[0], data)
+    assert np.array_equal(got[1], data[12345:12345 + 10_000_000])
+    assert np.array_equal(got[2], data[-4096:])
+    with pytest.raises(RuntimeError, match="expected"):
+        ext.load_file_async(str(path), data.size + 10).wait()  # short read
+    ext.prefetch_file(str(path), data.size)
+    ext.prefetch_file(str(path), 8192, 4096)
+    h = ext.load_file(str(path), data.size)
+    r = ext.load_file_region(str(path), 8192, 4096)
+    assert np.array_equal(ext.view_tensor(h, [data.size], "int8", 0).cpu().numpy().view(np.uint8), data)
+    assert np.array_equal(ext.view_tensor(r, [8192], "int8", 0).cpu().numpy().view(np.uint8), data[4096:12288])
+    ext.shutdown()

@@ -1,7 +1,7 @@
-"""Expert-parallel MoE and tensor-parallel GEMV on 2 GPUs over NCCL, each
-rank's CUDA kernels + one all-reduce, against the single-GPU result computed
-on rank 0.  Skipped unless two GPUs are visible (a box with one GPU cannot
-run two NCCL ranks)."""
+"""Expert-parallel MoE and tensor-parallel GEMV on 2 and 4 GPUs over NCCL and
+over NVLink peer memory, each rank's CUDA kernels + the exchange, against the
+single-GPU result computed on every rank.  Each case is skipped unless that
+many GPUs are visible (a box with one GPU cannot run NCCL ranks)."""
 from __future__ import annotations
 
 import os
@@ -58,6 +58,7 @@ def _worker(rank, world, port, q):
         words = PeerWordAllReduce(8 * hidden)
         y_ep_words = ep.ExpertParallelMoE(local, top_k=10, allreduce=words)(x)
         res["ep_words_equal"] = torch.equal(y_ep_words, y_ep)
+        res["ep_words_diff"] = (y_ep_words.float() - y_ep.float()).abs().max().item()
         worst_w = 0.0
         for it, (nel, dt) in enumerate([(8 * hidden, torch.float32), (1000, torch.float32), (4096, torch.float16),
                                         (8 * hidden, torch.float32), (7, torch.float16)]):
@@ -214,16 +215,18 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_expert_and_tensor_parallel_on_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_and_tensor_parallel_on_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=300) for _ in range(2))
+    out = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -238,7 +241,9 @@ def test_expert_and_tensor_parallel_on_two_gpus():
         # peer all-reduce: fp32 sum vs NCCL's fp16 sum, relative to the value
         assert res["p2p"] <= 2e-3, (rank, res)
         assert res["p2p_err"] == 0, (rank, res)
-        assert res["ep_words_equal"], (rank, res)
+        # two ranks: NCCL adds a + b as the word all-reduce does (same bits);
+        # more ranks: NCCL's order may differ, one fp16 rounding apart
+        assert res["ep_words_equal"] or (world > 2 and res["ep_words_diff"] <= 2e-3 * res["ep_scale"] + 1e-3), (rank, res)
         assert res["words"] <= 1e-3, (rank, res)   # fp32 rank-order sum vs NCCL (fp16 inputs summed in fp32)
         assert res["words_err"] == 0, (rank, res)
         # fused row split: fp32 partials summed in rank order then one fp16
