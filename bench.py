@@ -424,7 +424,7 @@ def config1_model_dir(device) -> str:
     return _MODEL_DIR
 
 
-def e2e_decode(dist, module: str, scheduler_ops: bool = False):
+def e2e_decode(dist, module: str, scheduler_ops: bool = False, graph: bool = False):
     """Greedy decode through GdsLLM's own CachedScheduler (the reference
     package in baseline/_ref, unchanged): prompt of 509 tokens, 3 untimed
     decode steps (KV prefilled to 512 positions), then 128 timed tokens, each
@@ -433,7 +433,11 @@ def e2e_decode(dist, module: str, scheduler_ops: bool = False):
     scheduler imports: "ours" (this build) or "reference" (GdsLLM's kernels
     compiled unchanged, oracle/ref_module.py -- the reference arm only).
     ``scheduler_ops`` also installs gdsllm_b200.scheduler_ops (embedding row
-    gather, fused lm_head) into the scheduler module."""
+    gather, fused lm_head) into the scheduler module.  ``graph`` decodes the
+    timed tokens with gdsllm_b200.decode_step.GraphDecodeStep built from the
+    same scheduler and KV cache after the same prefill: one CUDA graph replay
+    per token, the token id copied to pinned host memory inside the graph
+    and read by the host every step."""
     if not (REF_PACKAGE / "gdsllm" / "runtime" / "scheduler.py").exists():
         return {"unavailable": "the reference package is not installed in baseline/_ref"}
     if str(REF_PACKAGE) not in sys.path:
@@ -461,32 +465,48 @@ def e2e_decode(dist, module: str, scheduler_ops: bool = False):
             logits = s.forward(prompt, kv_cache=kv, start_pos=0)
             tok = int(logits[0, -1].argmax())
             pos = prompt.shape[1]
+            if graph:
+                from gdsllm_b200.decode_step import GraphDecodeStep
+                step = GraphDecodeStep.from_scheduler(s, kv)
+                step.reset(tok, pos)
+                step.capture()
+                launches = step.launches_per_step()
+                advance = step.step  # one replay; the host reads the token from pinned memory
+            else:
+                launches = None
+
+                def advance():
+                    nonlocal tok, pos
+                    logits = s.forward(torch.tensor([[tok]]), kv_cache=kv, start_pos=pos)
+                    tok = int(logits[0, -1].argmax())  # D2H of the step's result
+                    pos += 1
+                    return tok
             for _ in range(DECODE_WARMUP):
-                logits = s.forward(torch.tensor([[tok]]), kv_cache=kv, start_pos=pos)
-                tok = int(logits[0, -1].argmax())
-                pos += 1
+                advance()
             torch.cuda.synchronize()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0 = time.perf_counter()
             start.record()
             for _ in range(DECODE_TOKENS):
-                logits = s.forward(torch.tensor([[tok]]), kv_cache=kv, start_pos=pos)
-                tok = int(logits[0, -1].argmax())  # D2H of the step's result
-                tokens.append(tok)
-                pos += 1
+                tokens.append(advance())
             end.record()
             torch.cuda.synchronize()
             wall = time.perf_counter() - t0
             ms = start.elapsed_time(end)
+            if graph:
+                del step, advance
     finally:
         sched_mod._embed_tokens, sched_mod._lm_head_proj = saved
     return {"value": round(DECODE_TOKENS / (ms / 1e3), 2), "unit": "tok/s", "ms_per_token": round(ms / DECODE_TOKENS, 4),
             "wall_s": round(wall, 3), "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
             "tokens_head": tokens[:8],
+            **({"gpu_launches_per_token": launches} if graph else {}),
             "what": ("GdsLLM's CachedScheduler + llama.transformer_block unchanged (baseline/_ref), config 1: 32 layers "
                      "Q4_0, Q8_0 lm_head, fp16 embedding, KV prefilled to 512, 128 greedy tokens; gds_io_ext = "
                      + ("this build" if module == "ours" else "GdsLLM's own kernels (oracle/ref_module.py)")
-                     + ("; embedding and lm_head through gdsllm_b200.scheduler_ops" if scheduler_ops else ""))}
+                     + ("; embedding and lm_head through gdsllm_b200.scheduler_ops" if scheduler_ops else "")
+                     + ("; prefill by the scheduler, then every token one replay of "
+                        "gdsllm_b200.decode_step.GraphDecodeStep (CUDA graph) on the same KV cache" if graph else ""))}
 
 
 def _summary(res: dict, keys) -> dict:
@@ -650,6 +670,7 @@ def bench_ours(args, dist):
         if dist.world == 1:  # the scheduler loads onto one GPU
             result["e2e_decode"] = e2e_decode(dist, "ours")
             result["e2e_decode_scheduler_ops"] = e2e_decode(dist, "ours", scheduler_ops=True)
+            result["e2e_decode_graph"] = e2e_decode(dist, "ours", graph=True)
         del tok
         torch.cuda.empty_cache()
         result.update(sub_benches(args, dist))

@@ -159,3 +159,65 @@ def moe_route(logits: torch.Tensor, top_k: int, x: torch.Tensor | None = None,
     check(lib().gdsq_moe_route(_p(logits), ntok, e, top_k, _p(x), _p(shared_gate), hidden, _p(ids), _p(w), _p(sw),
                                _stream(logits)), "gdsq_moe_route")
     return ids, w, sw
+
+
+# ---- decode step (batch 1, position in device memory) ----------------------
+
+def add_rmsnorm(h: torch.Tensor, weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
+                h_out: torch.Tensor | None = None, out=None) -> torch.Tensor:
+    """h_out = h + delta (when delta is given; h_out defaults to h, in place),
+    then rms_norm(h_out) * weight (llama.py:17-23) into `out`."""
+    hidden = weight.numel()
+    rows = h.numel() // hidden
+    out = _out(out, h.shape, h)
+    if delta is not None and h_out is None:
+        h_out = h
+    check(lib().gdsq_add_rmsnorm_f16(_p(h), _p(delta), _p(h_out), _p(weight), _p(out), rows, hidden, float(eps),
+                                     _stream(h)), "gdsq_add_rmsnorm_f16")
+    return out
+
+
+def rope_kv(q, k, v, q_out, freqs: torch.Tensor, pos: torch.Tensor, k_cache, v_cache, num_heads: int,
+            num_kv_heads: int, head_dim: int, max_seq: int) -> torch.Tensor:
+    """RoPE of q into q_out and of k into k_cache[:, *pos], v into
+    v_cache[:, *pos]; freqs is view_as_real(freqs_cis) (fp32 pairs)."""
+    check(lib().gdsq_rope_kv_f16(_p(q), _p(k), _p(v), _p(q_out), _p(freqs), _p(pos), _p(k_cache), _p(v_cache),
+                                 num_heads, num_kv_heads, head_dim, max_seq, _stream(q)), "gdsq_rope_kv_f16")
+    return q_out
+
+
+def attention_scale(head_dim: int) -> float:
+    """The fp32 factor torch multiplies by for `scores / head_dim ** 0.5`."""
+    import numpy as np
+    return float(np.float32(1.0) / np.float32(head_dim ** 0.5))
+
+
+def attention_decode(q, k_cache, v_cache, pos: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int,
+                     max_seq: int, out=None) -> torch.Tensor:
+    out = _out(out, (num_heads * head_dim,), q)
+    check(lib().gdsq_attention_decode_f16(_p(q), _p(k_cache), _p(v_cache), _p(pos), _p(out), num_heads,
+                                          num_kv_heads, head_dim, max_seq, attention_scale(head_dim), _stream(q)),
+          "gdsq_attention_decode_f16")
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out=None) -> torch.Tensor:
+    out = _out(out, gate.shape, gate)
+    check(lib().gdsq_silu_mul_f16(_p(gate), _p(up), _p(out), gate.numel(), _stream(gate)), "gdsq_silu_mul_f16")
+    return out
+
+
+def argmax(logits: torch.Tensor, token: torch.Tensor, pos: torch.Tensor | None = None) -> torch.Tensor:
+    """token[0] = first index of the largest logit; pos[0] += 1 if given."""
+    check(lib().gdsq_argmax_f16(_p(logits), logits.numel(), _p(token), _p(pos), _stream(logits)), "gdsq_argmax_f16")
+    return token
+
+
+def dequant_rows(fmt: str, table: torch.Tensor, rows: int, cols: int, ids: torch.Tensor, out=None) -> torch.Tensor:
+    """fp16 [len(ids), cols]: the GGUF table rows `ids` (int64, on the device),
+    dequantized; an id outside [0, rows) gives a zero row and device error
+    bit 4."""
+    out = _out(out, (ids.numel(), cols), table)
+    check(lib().gdsq_dequant_rows_gguf(0 if fmt == "q4_0" else 1, _p(table), rows, cols, _p(ids), ids.numel(),
+                                       _p(out), _stream(table)), "gdsq_dequant_rows_gguf")
+    return out

@@ -23,6 +23,7 @@
 #include "gemv_tcb.cuh"
 #include "moe.cuh"
 #include "p2p.cuh"
+#include "decode.cuh"
 
 namespace gdsq {
 namespace {
@@ -1517,6 +1518,135 @@ int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_
              static_cast<const __half*>(x), static_cast<const __half*>(shared_gate), hidden_dim, expert_ids,
              static_cast<__half*>(route_weights), static_cast<__half*>(shared_weights));
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "moe route launch");
+}
+
+// ---------------------------------------------------------------------------
+// Decode-step kernels (decode.cuh): the non-GEMV work of one LLaMA decode
+// position, position in device memory, for a graph-captured token.
+
+int gdsq_add_rmsnorm_f16(const void* h_in, const void* delta, void* h_out, const void* weight, void* x_out,
+                         int rows, int hidden, float eps, void* stream_v) {
+  t_last_error.clear();
+  if (rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > kNormThreads * 8 * kNormMaxChunks)
+    return fail(GDSQ_ERR_INVALID_VALUE, "add_rmsnorm: hidden %d must be a positive multiple of 8 up to %d, rows %d",
+                hidden, kNormThreads * 8 * kNormMaxChunks, rows);
+  if (rows == 0) return GDSQ_OK;
+  if (!h_in || !weight || !x_out || (delta && !h_out)) return fail(GDSQ_ERR_INVALID_VALUE, "add_rmsnorm: null pointer");
+  if (!aligned(h_in, 16) || !aligned(weight, 16) || !aligned(x_out, 16) ||
+      (delta && (!aligned(delta, 16) || !aligned(h_out, 16))))
+    return fail(GDSQ_ERR_MISALIGNED, "add_rmsnorm: every pointer must be 16-byte aligned");
+  cudaError_t e = launch(add_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream_v),
+                         g_pdl_enabled != 0, static_cast<const __half*>(h_in), static_cast<const __half*>(delta),
+                         static_cast<__half*>(h_out), static_cast<const __half*>(weight), static_cast<__half*>(x_out),
+                         hidden, 1.0f / static_cast<float>(hidden), eps);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "add_rmsnorm launch");
+}
+
+int gdsq_rope_kv_f16(const void* q, const void* k, const void* v, void* q_out, const void* freqs,
+                     const long long* pos, void* k_cache, void* v_cache, int num_heads, int num_kv_heads,
+                     int head_dim, int max_seq, void* stream_v) {
+  t_last_error.clear();
+  if (num_heads < 1 || num_kv_heads < 1 || head_dim < 2 || head_dim % 2 != 0 || head_dim > 2048 || max_seq < 1)
+    return fail(GDSQ_ERR_INVALID_VALUE, "rope_kv: heads %d / kv heads %d, head_dim %d (even, <= 2048), max_seq %d",
+                num_heads, num_kv_heads, head_dim, max_seq);
+  if (!q || !k || !v || !q_out || !freqs || !pos || !k_cache || !v_cache)
+    return fail(GDSQ_ERR_INVALID_VALUE, "rope_kv: null pointer");
+  if (!aligned(q, 4) || !aligned(k, 4) || !aligned(v, 4) || !aligned(q_out, 4) || !aligned(k_cache, 4) ||
+      !aligned(v_cache, 4) || !aligned(freqs, 8) || !aligned(pos, 8))
+    return fail(GDSQ_ERR_MISALIGNED, "rope_kv: fp16 pointers 4-byte, freqs and pos 8-byte alignment");
+  cudaError_t e = launch(rope_kv_kernel, dim3(num_heads + num_kv_heads), dim3(head_dim / 2), 0,
+                         static_cast<cudaStream_t>(stream_v), g_pdl_enabled != 0, static_cast<const __half*>(q),
+                         static_cast<const __half*>(k), static_cast<const __half*>(v), static_cast<__half*>(q_out),
+                         static_cast<const float2*>(freqs), pos, static_cast<__half*>(k_cache),
+                         static_cast<__half*>(v_cache), num_heads, head_dim, max_seq);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "rope_kv launch");
+}
+
+int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_cache, const long long* pos,
+                              void* out, int num_heads, int num_kv_heads, int head_dim, int max_seq, float scale,
+                              void* stream_v) {
+  t_last_error.clear();
+  if (num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0 || (head_dim != 64 && head_dim != 128) ||
+      max_seq < 1)
+    return fail(GDSQ_ERR_INVALID_VALUE, "attention: heads %d must be a multiple of kv heads %d, head_dim %d "
+                "(64 or 128), max_seq %d", num_heads, num_kv_heads, head_dim, max_seq);
+  if (!q || !k_cache || !v_cache || !pos || !out) return fail(GDSQ_ERR_INVALID_VALUE, "attention: null pointer");
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 2) || !aligned(pos, 8))
+    return fail(GDSQ_ERR_MISALIGNED, "attention: q and the caches 16-byte, pos 8-byte alignment");
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  // About two CTAs per SM: the cluster (<= 8) splits each head's positions.
+  int C = 1;
+  while (C < 8 && 2 * C * num_heads <= 2 * dev->sms && 2 * C <= max_seq) C *= 2;
+  const int cap = (max_seq + C - 1) / C;
+  const int slices = head_dim / 8;
+  const int groups = kDecodeThreads / slices;
+  const size_t floats = (size_t)((cap + 3) & ~3) + (size_t)groups * head_dim + (size_t)C * head_dim +
+                        2 * kAttnMaxCluster + 2 * (kDecodeThreads / 32);
+  const size_t smem = floats * sizeof(float);
+  if (smem > (size_t)dev->smem_optin)
+    return fail(GDSQ_ERR_UNSUPPORTED, "attention: max_seq %d needs %zu bytes of shared memory", max_seq, smem);
+  auto kernel = head_dim == 128 ? attn_decode_kernel<128> : attn_decode_kernel<64>;
+  cudaError_t e = ensure_smem(kernel, (int)smem, dev->ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, num_heads);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream_v);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (g_pdl_enabled) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const __half*>(q), static_cast<const __half*>(k_cache),
+                         static_cast<const __half*>(v_cache), pos, static_cast<__half*>(out), num_heads, num_kv_heads,
+                         max_seq, scale);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "attention launch");
+}
+
+int gdsq_silu_mul_f16(const void* gate, const void* up, void* out, long long n, void* stream_v) {
+  t_last_error.clear();
+  if (n < 0) return fail(GDSQ_ERR_INVALID_VALUE, "silu_mul: negative size");
+  if (n == 0) return GDSQ_OK;
+  if (!gate || !up || !out) return fail(GDSQ_ERR_INVALID_VALUE, "silu_mul: null pointer");
+  if (!aligned(gate, 2) || !aligned(up, 2) || !aligned(out, 2))
+    return fail(GDSQ_ERR_MISALIGNED, "silu_mul: fp16 pointers must be 2-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  const bool vec = n % 8 == 0 && aligned(gate, 16) && aligned(up, 16) && aligned(out, 16);
+  const long long units = vec ? n / 8 : n;
+  const unsigned grid = (unsigned)std::min<long long>((units + kDecodeThreads - 1) / kDecodeThreads,
+                                                      (long long)dev->sms * 8);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const __half* g = static_cast<const __half*>(gate);
+  const __half* u = static_cast<const __half*>(up);
+  __half* o = static_cast<__half*>(out);
+  cudaError_t e = vec ? launch(silu_mul_kernel<true>, dim3(grid), dim3(kDecodeThreads), 0, stream, g_pdl_enabled != 0,
+                               g, u, o, n)
+                      : launch(silu_mul_kernel<false>, dim3(grid), dim3(kDecodeThreads), 0, stream,
+                               g_pdl_enabled != 0, g, u, o, n);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "silu_mul launch");
+}
+
+int gdsq_argmax_f16(const void* logits, int n, long long* token, long long* pos, void* stream_v) {
+  t_last_error.clear();
+  if (n < 1) return fail(GDSQ_ERR_INVALID_VALUE, "argmax: n %d < 1", n);
+  if (!logits || !token) return fail(GDSQ_ERR_INVALID_VALUE, "argmax: null pointer");
+  if (!aligned(logits, 2) || !aligned(token, 8) || (pos && !aligned(pos, 8)))
+    return fail(GDSQ_ERR_MISALIGNED, "argmax: logits 2-byte, token and pos 8-byte alignment");
+  cudaError_t e = launch(argmax_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream_v),
+                         g_pdl_enabled != 0, static_cast<const __half*>(logits), n, token, pos);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "argmax launch");
 }
 
 }  // extern "C"

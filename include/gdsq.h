@@ -270,6 +270,46 @@ GDSQ_API int gdsq_moe_route(const void* logits, int num_tokens, int num_experts,
                             const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
                             void* shared_weights, void* stream);
 
+/* ---- Decode step (batch 1, position in device memory) --------------------
+ * The work of one LLaMA decode position around the fused GEMVs, so that a
+ * whole token can be captured as one CUDA graph.  No reference launcher:
+ * these replace the torch code of llama.py's transformer_block at decode,
+ * in the same arithmetic order.  pos points to one int64 on the device;
+ * a position outside [0, max_seq) sets device error bit 4 and nothing is
+ * written. */
+
+/* h_out = h_in + delta (fp16 add; skipped when delta is NULL), then
+ * x_out = fp16(fp16(h * rsqrt(mean(h^2) + eps)) * weight) per row of
+ * `hidden` elements (llama.py:17-23, 285-293).  hidden % 8 == 0, <= 16384;
+ * 16-byte aligned pointers; h_out may equal h_in. */
+GDSQ_API int gdsq_add_rmsnorm_f16(const void* h_in, const void* delta, void* h_out, const void* weight, void* x_out,
+                                  int rows, int hidden, float eps, void* stream);
+
+/* RoPE (llama.py:83-105) of q [num_heads][head_dim] into q_out and of k
+ * [num_kv_heads][head_dim] into k_cache at *pos, v copied into v_cache at
+ * *pos (KVCache.update, kv_cache.py:44-67).  freqs: float pairs
+ * [max_seq][head_dim/2] (view_as_real of precompute_freqs_cis); caches of
+ * one layer [num_kv_heads][max_seq][head_dim] fp16. */
+GDSQ_API int gdsq_rope_kv_f16(const void* q, const void* k, const void* v, void* q_out, const void* freqs,
+                              const long long* pos, void* k_cache, void* v_cache, int num_heads, int num_kv_heads,
+                              int head_dim, int max_seq, void* stream);
+
+/* out [num_heads][head_dim] = softmax(fp16(fp16(q.K^T) * scale)) V over the
+ * positions [0, *pos] of the layer's caches (llama.py:228-242), query head h
+ * reading KV head h / (num_heads / num_kv_heads).  scale is the fp32
+ * reciprocal torch uses for `scores / sqrt(head_dim)`:
+ * 1.0f / (float)sqrt(head_dim).  head_dim 64 or 128. */
+GDSQ_API int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_cache, const long long* pos,
+                                       void* out, int num_heads, int num_kv_heads, int head_dim, int max_seq,
+                                       float scale, void* stream);
+
+/* out = fp16(silu(gate)) * up, n elements (llama.py:248-252). */
+GDSQ_API int gdsq_silu_mul_f16(const void* gate, const void* up, void* out, long long n, void* stream);
+
+/* *token = the first index of the largest of n fp16 logits (torch.argmax);
+ * then *pos += 1 when pos is not NULL. */
+GDSQ_API int gdsq_argmax_f16(const void* logits, int n, long long* token, long long* pos, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
