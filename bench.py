@@ -1060,13 +1060,19 @@ def main():
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--decode", choices=["scheduler", "scheduler_ops", "graph"], default=None,
+                    help="only the end-to-end config 1 decode (e2e_decode*): through the reference scheduler, "
+                         "with scheduler_ops, or with the graph-captured decode step")
     ap.add_argument("--quick", action="store_true",
                     help="default line only: skip the scheduler decode and the config 0 / 3 / 4 sub-benchmarks")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     dist = Dist(sample_clocks=args.impl != "reference")
     try:
-        if args.impl == "reference":
+        if args.decode is not None:
+            res = e2e_decode(dist, "ours" if args.impl == "ours" else "reference",
+                             scheduler_ops=args.decode == "scheduler_ops", graph=args.decode == "graph")
+        elif args.impl == "reference":
             res = bench_reference(args, dist)
         elif args.config == 0:
             res = bench_config0(args, dist)

@@ -60,6 +60,8 @@ _C_SIGNATURES = {
     "gdsq_rope_kv_f16": (ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
     "gdsq_attention_decode_f16": (ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 +
                                   [ctypes.c_float, ctypes.c_void_p]),
+    "gdsq_attention_decode_rope_f16": (ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4 +
+                                       [ctypes.c_float, ctypes.c_void_p]),
     "gdsq_silu_mul_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                          ctypes.c_void_p]),
     "gdsq_argmax_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,

@@ -201,6 +201,18 @@ def attention_decode(q, k_cache, v_cache, pos: torch.Tensor, num_heads: int, num
     return out
 
 
+def attention_decode_rope(q, k, v, freqs: torch.Tensor, pos: torch.Tensor, k_cache, v_cache, num_heads: int,
+                          num_kv_heads: int, head_dim: int, max_seq: int, out=None) -> torch.Tensor:
+    """attention_decode with the RoPE of q and k and the cache write of k
+    and v at *pos folded in (q, k, v before RoPE)."""
+    out = _out(out, (num_heads * head_dim,), q)
+    check(lib().gdsq_attention_decode_rope_f16(_p(q), _p(k), _p(v), _p(freqs), _p(pos), _p(k_cache), _p(v_cache),
+                                               _p(out), num_heads, num_kv_heads, head_dim, max_seq,
+                                               attention_scale(head_dim), _stream(q)),
+          "gdsq_attention_decode_rope_f16")
+    return out
+
+
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out=None) -> torch.Tensor:
     out = _out(out, gate.shape, gate)
     check(lib().gdsq_silu_mul_f16(_p(gate), _p(up), _p(out), gate.numel(), _stream(gate)), "gdsq_silu_mul_f16")
@@ -221,3 +233,4 @@ def dequant_rows(fmt: str, table: torch.Tensor, rows: int, cols: int, ids: torch
     check(lib().gdsq_dequant_rows_gguf(0 if fmt == "q4_0" else 1, _p(table), rows, cols, _p(ids), ids.numel(),
                                        _p(out), _stream(table)), "gdsq_dequant_rows_gguf")
     return out
+

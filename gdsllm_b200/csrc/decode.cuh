@@ -164,11 +164,20 @@ __global__ void rope_kv_kernel(const __half* __restrict__ q, const __half* __res
 // shared memory, each adds its probability-weighted V rows, and CTA 0 of the
 // cluster adds the C partial outputs in rank order.  Shared memory (floats):
 // scores [ceil(max_seq / C)] | group partials [256/(HD/8)][HD] |
-// cluster partials [C][HD] | maxima [16] | sums [16] | reductions [2][8].
-template <int HD>
+// cluster partials [C][HD] | maxima [16] | sums [16] | reductions [2][8] |
+// (kRope) the new K and V rows [HD] fp16 each.
+//
+// kRope: q, k_new and v_new are the projections before RoPE (rope_kv_kernel
+// folded in).  Every lane rotates its own q elements; the CTA whose
+// positions include *pos rotates k_new of its KV head, writes it and v_new
+// into the caches at *pos and uses those rows from shared memory (CTAs of
+// other query heads of the same KV head write the same values).  Without
+// kRope, q is already rotated and row *pos is in the caches.
+template <int HD, bool kRope>
 __global__ void __launch_bounds__(kDecodeThreads)
-    attn_decode_kernel(const __half* __restrict__ q, const __half* __restrict__ k_cache,
-                       const __half* __restrict__ v_cache, const long long* __restrict__ pos_p,
+    attn_decode_kernel(const __half* __restrict__ q, const __half* __restrict__ k_new,
+                       const __half* __restrict__ v_new, const float2* __restrict__ freqs,
+                       __half* k_cache, __half* v_cache, const long long* __restrict__ pos_p,
                        __half* __restrict__ out, int num_heads, int num_kv_heads, int max_seq, float scale) {
   constexpr int kPer = HD / 8;            // q / k elements per lane (8 lanes per position)
   constexpr int kVec = kPer / 8;          // 16-byte loads per lane per position
@@ -187,8 +196,10 @@ __global__ void __launch_bounds__(kDecodeThreads)
   float* xmax = cacc + C * HD;
   float* xsum = xmax + kAttnMaxCluster;
   float* red = xsum + kAttnMaxCluster;
-  const __half* kh_base = k_cache + (size_t)kvh * max_seq * HD;
-  const __half* vh_base = v_cache + (size_t)kvh * max_seq * HD;
+  __half* krow = reinterpret_cast<__half*>(red + 2 * kWarps);  // 16-byte aligned (offsets are multiples of 4 floats)
+  __half* vrow = krow + HD;
+  __half* kh_base = k_cache + (size_t)kvh * max_seq * HD;
+  __half* vh_base = v_cache + (size_t)kvh * max_seq * HD;
 
   if (C > 1) cluster_arrive_relaxed();  // waited for before the first DSMEM store
   // Warm L2 with this CTA's K and V rows while the producers finish.  The
@@ -223,10 +234,27 @@ __global__ void __launch_bounds__(kDecodeThreads)
   const int per = (L + C - 1) / C;
   const int j0 = c * per;
   const int n = max(0, min(L, j0 + per) - j0);
+  const int jnew = (int)pos - j0;  // slice-local index of the new row (valid when < n)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 3;
   const int s = lane & 7;
+
+  if constexpr (kRope) {
+    if (jnew < n && (int)threadIdx.x < HD / 2) {
+      const int i = threadIdx.x;
+      const float2 f = freqs[(size_t)pos * (HD / 2) + i];
+      const float2 a = __half22float2(reinterpret_cast<const __half2*>(k_new + (size_t)kvh * HD)[i]);
+      // (a.x + i a.y)(f.x + i f.y), as c10::complex<float> multiplies
+      const __half2 kr = __floats2half2_rn(a.x * f.x - a.y * f.y, a.x * f.y + a.y * f.x);
+      const __half2 vv = reinterpret_cast<const __half2*>(v_new + (size_t)kvh * HD)[i];
+      reinterpret_cast<__half2*>(krow)[i] = kr;
+      reinterpret_cast<__half2*>(vrow)[i] = vv;
+      reinterpret_cast<__half2*>(kh_base + (size_t)pos * HD)[i] = kr;
+      reinterpret_cast<__half2*>(vh_base + (size_t)pos * HD)[i] = vv;
+    }
+    __syncthreads();
+  }
 
   // Scores: each group of 8 lanes takes one position per pass.
   float qv[kPer];
@@ -239,18 +267,35 @@ __global__ void __launch_bounds__(kDecodeThreads)
 #pragma unroll
       for (int e = 0; e < 8; ++e) qv[8 * u + e] = t[e];
     }
+    if constexpr (kRope) {
+#pragma unroll
+      for (int e = 0; e < kPer; e += 2) {
+        const float2 f = freqs[(size_t)pos * (HD / 2) + (s * kPer + e) / 2];
+        const float a = qv[e], b = qv[e + 1];
+        const __half2 r = __floats2half2_rn(a * f.x - b * f.y, a * f.y + b * f.x);
+        const float2 rf = __half22float2(r);
+        qv[e] = rf.x;
+        qv[e + 1] = rf.y;
+      }
+    }
   }
   const __half* kb = kh_base + (size_t)j0 * HD + s * kPer;
+  auto krow_ptr = [&](int jj) -> const __half* {
+    if (kRope && jj == jnew) return krow + s * kPer;
+    return kb + (size_t)jj * HD;
+  };
   float lmax = -INFINITY;
   for (int b0 = warp * 4; b0 < n; b0 += 2 * kWarps * 4) {
     const int ja = b0 + g;
     const int jb = ja + kWarps * 4;
     const bool va = ja < n, vb = jb < n;
     uint4 ka[kVec], kbv[kVec];
+    const __half* pa = krow_ptr(ja);
+    const __half* pb = krow_ptr(jb);
 #pragma unroll
     for (int u = 0; u < kVec; ++u) {
-      ka[u] = va ? reinterpret_cast<const uint4*>(kb + (size_t)ja * HD)[u] : make_uint4(0, 0, 0, 0);
-      kbv[u] = vb ? reinterpret_cast<const uint4*>(kb + (size_t)jb * HD)[u] : make_uint4(0, 0, 0, 0);
+      ka[u] = va ? reinterpret_cast<const uint4*>(pa)[u] : make_uint4(0, 0, 0, 0);
+      kbv[u] = vb ? reinterpret_cast<const uint4*>(pb)[u] : make_uint4(0, 0, 0, 0);
     }
     float da = 0.f, db = 0.f;
 #pragma unroll
@@ -320,10 +365,14 @@ __global__ void __launch_bounds__(kDecodeThreads)
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
   const __half* vb0 = vh_base + (size_t)j0 * HD + slice * 8;
+  auto vrow_ptr = [&](int jj) -> const __half* {
+    if (kRope && jj == jnew) return vrow + slice * 8;
+    return vb0 + (size_t)jj * HD;
+  };
   for (int ja = grp; ja < n; ja += 2 * kGroups) {
     const int jb = ja + kGroups;
-    const uint4 a = *reinterpret_cast<const uint4*>(vb0 + (size_t)ja * HD);
-    const uint4 b = jb < n ? *reinterpret_cast<const uint4*>(vb0 + (size_t)jb * HD) : make_uint4(0, 0, 0, 0);
+    const uint4 a = *reinterpret_cast<const uint4*>(vrow_ptr(ja));
+    const uint4 b = jb < n ? *reinterpret_cast<const uint4*>(vrow_ptr(jb)) : make_uint4(0, 0, 0, 0);
     const float pa = sc[ja];
     const float pb = jb < n ? sc[jb] : 0.f;
     float ta[8], tb[8];
@@ -385,7 +434,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
 
 // One CTA of 1024 threads: token = the first index of the largest logit
 // (torch.argmax's tie rule; a NaN is skipped), then *pos += 1 when pos is
-// given.
+// given.  kVec: 8 logits per 16-byte load (n % 8 == 0, 16-byte aligned).
+template <bool kVec>
 __global__ void __launch_bounds__(1024)
     argmax_kernel(const __half* __restrict__ logits, int n, long long* __restrict__ token, long long* pos) {
   __shared__ float bv[32];
@@ -394,12 +444,21 @@ __global__ void __launch_bounds__(1024)
   pdl_wait_primary();
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = __half2float(logits[i]);
-    if (v > best || (idx == 0x7fffffff && v == best)) {  // strided order: the first index wins ties
+  auto take = [&](float v, int i) {  // indices arrive in increasing order per thread
+    if (v > best || (idx == 0x7fffffff && v == best)) {
       best = v;
       idx = i;
     }
+  };
+  if constexpr (kVec) {
+    for (int u = threadIdx.x; u < n / 8; u += blockDim.x) {
+      float t[8];
+      unpack8(reinterpret_cast<const uint4*>(logits)[u], t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) take(t[e], 8 * u + e);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) take(__half2float(logits[i]), i);
   }
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) {

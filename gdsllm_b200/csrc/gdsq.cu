@@ -378,12 +378,32 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
       const int v = atoi(cap);
       if (v >= 1 && v < occ) occ = v;
     }
-    const long long slots = (long long)dev.sms * occ;
+    long long slots = (long long)dev.sms * occ;
+    int st_pick = c.st;
+    int smem_pick = L.total;
+    // More than one wave of CTAs, and at least 4 chunks per warp: a one-stage
+    // ring that fits every CTA at once streams faster (22016 x 4096, the
+    // grouped gate/up: 17.2 vs 20.4 us in a PDL chain; with 1-2 chunks per
+    // warp the second stage wins).
+    const int mw = ((C + c.cs - 1) / c.cs + kGemvWarps - 1) / kGemvWarps;
+    if (!forced && c.st == 2 && (long long)R * c.cs > slots && mw >= 4) {
+      const GemvSmemLayout L1 = gemv_smem_layout<F>(B, K, GS, c.cs, 1, c.cp);
+      e = ensure_smem(kernel, L1.total, dev.ordinal);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
+      int occ1 = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, kernel, kGemvWarps * 32, L1.total);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      if ((long long)R * c.cs <= (long long)dev.sms * occ1) {
+        st_pick = 1;
+        smem_pick = L1.total;
+        slots = (long long)dev.sms * occ1;
+      }
+    }
     out->cs = c.cs;
-    out->stages = c.st;
+    out->stages = st_pick;
     out->copy = c.cp;
     out->nclusters = (long long)R * c.cs <= slots ? R : (int)(slots / c.cs);
-    out->smem = L.total;
+    out->smem = smem_pick;
     if (TP && c.cs > 1) {
       // The finisher CTAs wait for rows of every other cluster, so the whole
       // grid must be resident at once: cap the clusters at what the GPU can
@@ -391,7 +411,7 @@ int make_plan(int N, int K, const DeviceInfo& dev, GemvPlan* out) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(out->nclusters * c.cs);
       cfg.blockDim = dim3(kGemvWarps * 32);
-      cfg.dynamicSmemBytes = L.total;
+      cfg.dynamicSmemBytes = smem_pick;
       cudaLaunchAttribute attr;
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = c.cs;
@@ -805,7 +825,7 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
     if (cs > C) break;
     if (forced && cs != force_cs) continue;
     const int cslice = (C + cs - 1) / cs;
-    for (int st = 2; st <= 4; ++st) {
+    for (int st = forced ? 1 : 2; st <= 4; ++st) {
       if (forced && st != force_st) continue;
       const MoeSmemLayout L = moe_smem_layout(C, GS, cs, st);
       if (L.total > dev.smem_optin) continue;
@@ -844,6 +864,35 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
     }
   }
   if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no MoE launch plan fits shared memory");
+  // As for the plain GEMV: when the chosen plan needs more than one wave of
+  // CTAs, a one-stage ring with at least 4 chunks per warp that holds every
+  // item at once is faster (config 4 gate/up at batch 1: 316.6 vs 303.8
+  // tok/s; at batch 8 no such plan fits and the model's choice stays).
+  if (!forced) {
+    int occ_pick = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pick, kernel, kGemvWarps * 32, out->smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if ((long long)items * out->cs > (long long)dev.sms * occ_pick) {
+      for (int cs = 1; cs <= out->cs; cs *= 2) {
+        const int mw = ((C + cs - 1) / cs + kGemvWarps - 1) / kGemvWarps;
+        if (mw < 4) continue;
+        const MoeSmemLayout L1 = moe_smem_layout(C, GS, cs, 1);
+        if (L1.total > dev.smem_optin) continue;
+        e = ensure_smem(kernel, L1.total, dev.ordinal);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(moe)");
+        int occ1 = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, kernel, kGemvWarps * 32, L1.total);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if ((long long)items * cs <= (long long)dev.sms * occ1) {
+          out->cs = cs;
+          out->stages = 1;
+          out->nclusters = items;
+          out->smem = L1.total;
+          break;
+        }
+      }
+    }
+  }
   return GDSQ_OK;
 }
 
@@ -1562,17 +1611,24 @@ int gdsq_rope_kv_f16(const void* q, const void* k, const void* v, void* q_out, c
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "rope_kv launch");
 }
 
-int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_cache, const long long* pos,
-                              void* out, int num_heads, int num_kv_heads, int head_dim, int max_seq, float scale,
-                              void* stream_v) {
-  t_last_error.clear();
+}  // extern "C"
+
+namespace gdsq {
+namespace {
+// Shared by the plain and the RoPE-folding attention entry points.
+int attention_launch(bool rope, const void* q, const void* k_new, const void* v_new, const void* freqs,
+                     const long long* pos, void* k_cache, void* v_cache, void* out, int num_heads, int num_kv_heads,
+                     int head_dim, int max_seq, float scale, void* stream_v) {
   if (num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0 || (head_dim != 64 && head_dim != 128) ||
       max_seq < 1)
     return fail(GDSQ_ERR_INVALID_VALUE, "attention: heads %d must be a multiple of kv heads %d, head_dim %d "
                 "(64 or 128), max_seq %d", num_heads, num_kv_heads, head_dim, max_seq);
-  if (!q || !k_cache || !v_cache || !pos || !out) return fail(GDSQ_ERR_INVALID_VALUE, "attention: null pointer");
-  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 2) || !aligned(pos, 8))
-    return fail(GDSQ_ERR_MISALIGNED, "attention: q and the caches 16-byte, pos 8-byte alignment");
+  if (!q || !k_cache || !v_cache || !pos || !out || (rope && (!k_new || !v_new || !freqs)))
+    return fail(GDSQ_ERR_INVALID_VALUE, "attention: null pointer");
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 2) || !aligned(pos, 8) ||
+      (rope && (!aligned(k_new, 4) || !aligned(v_new, 4) || !aligned(freqs, 8))))
+    return fail(GDSQ_ERR_MISALIGNED, "attention: q and the caches 16-byte, pos and freqs 8-byte, new K/V 4-byte "
+                "alignment");
   const DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
   if (st != GDSQ_OK) return st;
@@ -1583,11 +1639,12 @@ int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_
   const int slices = head_dim / 8;
   const int groups = kDecodeThreads / slices;
   const size_t floats = (size_t)((cap + 3) & ~3) + (size_t)groups * head_dim + (size_t)C * head_dim +
-                        2 * kAttnMaxCluster + 2 * (kDecodeThreads / 32);
+                        2 * kAttnMaxCluster + 2 * (kDecodeThreads / 32) + (rope ? head_dim : 0);
   const size_t smem = floats * sizeof(float);
   if (smem > (size_t)dev->smem_optin)
     return fail(GDSQ_ERR_UNSUPPORTED, "attention: max_seq %d needs %zu bytes of shared memory", max_seq, smem);
-  auto kernel = head_dim == 128 ? attn_decode_kernel<128> : attn_decode_kernel<64>;
+  auto kernel = rope ? (head_dim == 128 ? attn_decode_kernel<128, true> : attn_decode_kernel<64, true>)
+                     : (head_dim == 128 ? attn_decode_kernel<128, false> : attn_decode_kernel<64, false>);
   cudaError_t e = ensure_smem(kernel, (int)smem, dev->ordinal);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
   cudaLaunchConfig_t cfg = {};
@@ -1607,10 +1664,32 @@ int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.numAttrs = 2;
   }
-  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const __half*>(q), static_cast<const __half*>(k_cache),
-                         static_cast<const __half*>(v_cache), pos, static_cast<__half*>(out), num_heads, num_kv_heads,
-                         max_seq, scale);
+  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const __half*>(q), static_cast<const __half*>(k_new),
+                         static_cast<const __half*>(v_new), static_cast<const float2*>(freqs),
+                         static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), pos, static_cast<__half*>(out),
+                         num_heads, num_kv_heads, max_seq, scale);
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "attention launch");
+}
+}  // namespace
+}  // namespace gdsq
+
+extern "C" {
+
+int gdsq_attention_decode_f16(const void* q, const void* k_cache, const void* v_cache, const long long* pos,
+                              void* out, int num_heads, int num_kv_heads, int head_dim, int max_seq, float scale,
+                              void* stream_v) {
+  t_last_error.clear();
+  return attention_launch(false, q, nullptr, nullptr, nullptr, pos, const_cast<void*>(k_cache),
+                          const_cast<void*>(v_cache), out, num_heads, num_kv_heads, head_dim, max_seq, scale,
+                          stream_v);
+}
+
+int gdsq_attention_decode_rope_f16(const void* q, const void* k, const void* v, const void* freqs,
+                                   const long long* pos, void* k_cache, void* v_cache, void* out, int num_heads,
+                                   int num_kv_heads, int head_dim, int max_seq, float scale, void* stream_v) {
+  t_last_error.clear();
+  return attention_launch(true, q, k, v, freqs, pos, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim,
+                          max_seq, scale, stream_v);
 }
 
 int gdsq_silu_mul_f16(const void* gate, const void* up, void* out, long long n, void* stream_v) {
@@ -1644,8 +1723,10 @@ int gdsq_argmax_f16(const void* logits, int n, long long* token, long long* pos,
   if (!logits || !token) return fail(GDSQ_ERR_INVALID_VALUE, "argmax: null pointer");
   if (!aligned(logits, 2) || !aligned(token, 8) || (pos && !aligned(pos, 8)))
     return fail(GDSQ_ERR_MISALIGNED, "argmax: logits 2-byte, token and pos 8-byte alignment");
-  cudaError_t e = launch(argmax_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream_v),
-                         g_pdl_enabled != 0, static_cast<const __half*>(logits), n, token, pos);
+  const bool vec = n % 8 == 0 && aligned(logits, 16);
+  cudaError_t e = launch(vec ? argmax_kernel<true> : argmax_kernel<false>, dim3(1), dim3(1024), 0,
+                         static_cast<cudaStream_t>(stream_v), g_pdl_enabled != 0,
+                         static_cast<const __half*>(logits), n, token, pos);
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "argmax launch");
 }
 

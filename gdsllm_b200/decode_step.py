@@ -17,8 +17,8 @@ replayed per token:
     per layer:
         add_rmsnorm   (residual add of the previous MLP output + input norm)
         q/k/v         one grouped fused dequant-GEMV launch
-        rope_kv       RoPE of q and k, k and v written at the position
-        attention     split over positions by a thread-block cluster
+        attention     RoPE of q and k and the K/V write at the position folded
+                      in; positions split over a thread-block cluster
         o             fused dequant-GEMV
         add_rmsnorm   (residual add of the attention output + post norm)
         gate/up       one grouped fused dequant-GEMV launch
@@ -37,6 +37,11 @@ error bars, with the same greedy tokens (tests/test_decode_step_gpu.py).
 
 The kernels launch with programmatic dependent launch, so each one's
 prologue (for a GEMV, its weight stream) overlaps its predecessor's tail.
+That is also why the RMSNorm and SiLU*up stay kernels of their own: a
+one-CTA kernel between two GEMVs runs while the next GEMV's CTAs already
+stream their weights, whereas folding it into that GEMV's activation staging
+puts it on every CTA's path (measured 3 % slower per token for the norm,
+no gain for SiLU*up, on config 1).
 """
 from __future__ import annotations
 
@@ -96,7 +101,7 @@ class GraphDecodeStep:
     advances the position.  ``logits`` holds the last step's logits."""
 
     def __init__(self, layers, embed: dict, final_norm: torch.Tensor, lm_head: dict, freqs_cis: torch.Tensor,
-                 kv_cache, num_heads: int, num_kv_heads: int, rms_norm_eps: float):
+                 kv_cache, num_heads: int, num_kv_heads: int, rms_norm_eps: float, fused: bool = True):
         self.layers = [_Layer(t, i) for i, t in enumerate(layers)]
         if not self.layers:
             raise ValueError("GraphDecodeStep: no layers")
@@ -142,9 +147,10 @@ class GraphDecodeStep:
         self.d = torch.empty(self.hidden, **f16)
         self.logits = torch.empty(self.vocab, **f16)
         self.graph = None
+        self.fused = bool(fused) and self.head_dim in (64, 128)
 
     @classmethod
-    def from_scheduler(cls, sched, kv_cache) -> "GraphDecodeStep":
+    def from_scheduler(cls, sched, kv_cache, fused: bool = True) -> "GraphDecodeStep":
         """From an entered ``CachedScheduler`` (gdsllm/runtime/scheduler.py):
         every layer is taken from its layer cache and stays referenced here,
         so the buffers the graph reads stay allocated."""
@@ -158,7 +164,7 @@ class GraphDecodeStep:
             head = embed["model.embed_tokens.weight"]
         c = sched.config
         return cls(layers, embed, norm, head, sched.freqs_cis, kv_cache, c["num_heads"], c["num_kv_heads"],
-                   c["rms_norm_eps"])
+                   c["rms_norm_eps"], fused=fused)
 
     # -- the token's launches ------------------------------------------------
 
@@ -179,10 +185,14 @@ class GraphDecodeStep:
             capi.add_rmsnorm(self.h, lay.in_norm, self.eps, delta=self.d if i else None, out=self.x)
             self._project([lay.q, lay.k, lay.v], self.x, [q, k, v])
             kc, vc = self.kv.k_cache[i, 0], self.kv.v_cache[i, 0]
-            capi.rope_kv(q, k, v, self.q_rot, self.freqs, self.pos, kc, vc, self.num_heads, self.num_kv_heads,
-                         self.head_dim, self.max_seq)
-            capi.attention_decode(self.q_rot, kc, vc, self.pos, self.num_heads, self.num_kv_heads, self.head_dim,
-                                  self.max_seq, out=self.attn)
+            if self.fused:  # RoPE and the cache write inside the attention kernel
+                capi.attention_decode_rope(q, k, v, self.freqs, self.pos, kc, vc, self.num_heads, self.num_kv_heads,
+                                           self.head_dim, self.max_seq, out=self.attn)
+            else:
+                capi.rope_kv(q, k, v, self.q_rot, self.freqs, self.pos, kc, vc, self.num_heads, self.num_kv_heads,
+                             self.head_dim, self.max_seq)
+                capi.attention_decode(self.q_rot, kc, vc, self.pos, self.num_heads, self.num_kv_heads,
+                                      self.head_dim, self.max_seq, out=self.attn)
             _gemv(lay.o[0], lay.o[1], self.attn, lay.o[2], lay.o[3], self.o)
             capi.add_rmsnorm(self.h, lay.post_norm, self.eps, delta=self.o, out=self.x)
             self._project([lay.gate, lay.up], self.x, [gate, up])
@@ -209,7 +219,7 @@ class GraphDecodeStep:
         """Kernels of one token (the pinned copy of the token is not one)."""
         n = 1 + 3  # embedding; final norm, lm_head, argmax
         for lay in self.layers:
-            n += 6  # two norms, rope_kv, attention, o, silu_mul, down
+            n += 6 + (0 if self.fused else 1)  # two norms, (rope_kv), attention, o, silu_mul, down
             n += 1 if self._groupable([lay.q, lay.k, lay.v]) else 3
             n += 1 if self._groupable([lay.gate, lay.up]) else 2
         return n

@@ -303,6 +303,15 @@ GDSQ_API int gdsq_attention_decode_f16(const void* q, const void* k_cache, const
                                        void* out, int num_heads, int num_kv_heads, int head_dim, int max_seq,
                                        float scale, void* stream);
 
+/* The same attention with the RoPE and cache write of gdsq_rope_kv_f16
+ * folded in: q [num_heads][head_dim], k and v [num_kv_heads][head_dim] are
+ * the projections before RoPE; k (rotated) and v are written into the
+ * caches at *pos and attended to in the same launch. */
+GDSQ_API int gdsq_attention_decode_rope_f16(const void* q, const void* k, const void* v, const void* freqs,
+                                            const long long* pos, void* k_cache, void* v_cache, void* out,
+                                            int num_heads, int num_kv_heads, int head_dim, int max_seq, float scale,
+                                            void* stream);
+
 /* out = fp16(silu(gate)) * up, n elements (llama.py:248-252). */
 GDSQ_API int gdsq_silu_mul_f16(const void* gate, const void* up, void* out, long long n, void* stream);
 

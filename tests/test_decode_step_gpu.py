@@ -138,6 +138,31 @@ def test_attention_decode_matches_reference(cuda, nh, nkv, hd, max_seq):
     assert capi.device_error(0) == 0
 
 
+@pytest.mark.parametrize("nh,nkv,hd,max_seq", [(32, 32, 128, 640), (8, 2, 64, 200), (64, 8, 128, 1024)])
+def test_attention_with_rope_folded_in(cuda, nh, nkv, hd, max_seq):
+    """gdsq_attention_decode_rope_f16 = rope_kv then attention_decode: the
+    same cache rows (bit for bit) and outputs within the attention bar."""
+    g = torch.Generator().manual_seed(nh * 3 + max_seq)
+    q = torch.randn(nh * hd, generator=g).half().to(cuda)
+    k = torch.randn(nkv * hd, generator=g).half().to(cuda)
+    v = torch.randn(nkv * hd, generator=g).half().to(cuda)
+    freqs = torch.view_as_real(freqs_cis_ref(hd, max_seq, device=cuda)).contiguous()
+    kc = torch.randn(nkv, max_seq, hd, generator=g).half().to(cuda)
+    vc = torch.randn(nkv, max_seq, hd, generator=g).half().to(cuda)
+    for p in sorted({0, 1, max_seq // 3, max_seq - 1}):
+        pos = torch.tensor([p], dtype=torch.int64, device=cuda)
+        kc1, vc1 = kc.clone(), vc.clone()
+        q_rot = torch.empty_like(q)
+        capi.rope_kv(q, k, v, q_rot, freqs, pos, kc1, vc1, nh, nkv, hd, max_seq)
+        ref = capi.attention_decode(q_rot, kc1, vc1, pos, nh, nkv, hd, max_seq)
+        kc2, vc2 = kc.clone(), vc.clone()
+        out = capi.attention_decode_rope(q, k, v, freqs, pos, kc2, vc2, nh, nkv, hd, max_seq)
+        assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2), f"pos {p}: cache rows differ"
+        torch.testing.assert_close(out.float(), ref.float(), atol=4e-3, rtol=4e-3)
+    torch.cuda.synchronize()
+    assert capi.device_error(0) == 0
+
+
 def test_attention_position_outside_cache_sets_error(cuda):
     q = torch.zeros(4 * 64, dtype=torch.float16, device=cuda)
     kc = torch.zeros(4, 8, 64, dtype=torch.float16, device=cuda)
@@ -193,7 +218,8 @@ def reference():
     (dict(layers=2, hidden=512, heads=4, kv_heads=2, ffn=1536, vocab=2048, max_seq_len=64), "q4_0", "q8_0", "f16"),
     (dict(layers=3, hidden=512, heads=8, kv_heads=8, ffn=1024, vocab=1000, max_seq_len=40), "q8_0", "q4_0", "q4_0"),
 ])
-def test_graph_step_matches_cached_scheduler(reference, tmp_path, cuda, cfg, body, lm_head, embed):
+@pytest.mark.parametrize("fused", [True, False])
+def test_graph_step_matches_cached_scheduler(reference, tmp_path, cuda, cfg, body, lm_head, embed, fused):
     """Prefill through CachedScheduler.forward, then 12 greedy tokens twice:
     by CachedScheduler.forward per token (the reference loop) and by replays
     of the captured GraphDecodeStep on a second KV cache prefilled the same
@@ -223,7 +249,8 @@ def test_graph_step_matches_cached_scheduler(reference, tmp_path, cuda, cfg, bod
             tok = int(logits[0, -1].argmax())
             ref_tokens.append(tok)
             pos += 1
-        step = GraphDecodeStep.from_scheduler(sched, kvs[1])
+        step = GraphDecodeStep.from_scheduler(sched, kvs[1], fused=fused)
+        assert step.fused == fused
         step.reset(first[1], prompt.shape[1])
         step.capture()
         tokens, got = [], []
@@ -257,8 +284,9 @@ def test_graph_step_launch_count_and_rejects(cuda, tmp_path, reference):
     with torch.inference_mode(), sched_mod.CachedScheduler(str(tmp_path / "m"), device="cuda:0") as sched:
         c = sched.config
         kv = kv_mod.KVCache(c["num_layers"], c["num_kv_heads"], c["head_dim"], c["max_seq_len"], device=cuda)
-        step = GraphDecodeStep.from_scheduler(sched, kv)
-        assert step.launches_per_step() == 1 + 2 * 8 + 3
+        step = GraphDecodeStep.from_scheduler(sched, kv, fused=False)
+        assert step.launches_per_step() == 1 + 2 * 9 + 3
+        assert GraphDecodeStep.from_scheduler(sched, kv).launches_per_step() == 1 + 2 * 8 + 3
         with pytest.raises(ValueError, match="outside the KV cache"):
             step.reset(0, 32)
         bad = kv_mod.KVCache(c["num_layers"] + 1, c["num_kv_heads"], c["head_dim"], c["max_seq_len"], device=cuda)
