@@ -284,46 +284,45 @@ __global__ void __launch_bounds__(kDecodeThreads)
     if (kRope && jj == jnew) return krow + s * kPer;
     return kb + (size_t)jj * HD;
   };
+  // kUnroll positions per lane group per pass, all loads issued first.
+  constexpr int kUnroll = 4;
   float lmax = -INFINITY;
-  for (int b0 = warp * 4; b0 < n; b0 += 2 * kWarps * 4) {
-    const int ja = b0 + g;
-    const int jb = ja + kWarps * 4;
-    const bool va = ja < n, vb = jb < n;
-    uint4 ka[kVec], kbv[kVec];
-    const __half* pa = krow_ptr(ja);
-    const __half* pb = krow_ptr(jb);
+  for (int b0 = warp * 4; b0 < n; b0 += kUnroll * kWarps * 4) {
+    uint4 kv[kUnroll][kVec];
 #pragma unroll
-    for (int u = 0; u < kVec; ++u) {
-      ka[u] = va ? reinterpret_cast<const uint4*>(pa)[u] : make_uint4(0, 0, 0, 0);
-      kbv[u] = vb ? reinterpret_cast<const uint4*>(pb)[u] : make_uint4(0, 0, 0, 0);
+    for (int t = 0; t < kUnroll; ++t) {
+      const int jj = b0 + g + t * kWarps * 4;
+      const __half* pk = krow_ptr(jj);
+#pragma unroll
+      for (int u = 0; u < kVec; ++u)
+        kv[t][u] = jj < n ? reinterpret_cast<const uint4*>(pk)[u] : make_uint4(0, 0, 0, 0);
     }
-    float da = 0.f, db = 0.f;
+    float d[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kVec; ++u) {
-      float ta[8], tb[8];
-      unpack8(ka[u], ta);
-      unpack8(kbv[u], tb);
+    for (int t = 0; t < kUnroll; ++t) {
+      d[t] = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        da = fmaf(ta[e], qv[8 * u + e], da);
-        db = fmaf(tb[e], qv[8 * u + e], db);
+      for (int u = 0; u < kVec; ++u) {
+        float tk[8];
+        unpack8(kv[t][u], tk);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d[t] = fmaf(tk[e], qv[8 * u + e], d[t]);
       }
     }
 #pragma unroll
     for (int m = 4; m > 0; m >>= 1) {
-      da += __shfl_xor_sync(0xffffffffu, da, m);
-      db += __shfl_xor_sync(0xffffffffu, db, m);
+#pragma unroll
+      for (int t = 0; t < kUnroll; ++t) d[t] += __shfl_xor_sync(0xffffffffu, d[t], m);
     }
     if (s == 0) {
-      if (va) {
-        const float x = __half2float(__float2half_rn(__half2float(__float2half_rn(da)) * scale));
-        sc[ja] = x;
-        lmax = fmaxf(lmax, x);
-      }
-      if (vb) {
-        const float x = __half2float(__float2half_rn(__half2float(__float2half_rn(db)) * scale));
-        sc[jb] = x;
-        lmax = fmaxf(lmax, x);
+#pragma unroll
+      for (int t = 0; t < kUnroll; ++t) {
+        const int jj = b0 + g + t * kWarps * 4;
+        if (jj < n) {
+          const float x = __half2float(__float2half_rn(__half2float(__float2half_rn(d[t])) * scale));
+          sc[jj] = x;
+          lmax = fmaxf(lmax, x);
+        }
       }
     }
   }
@@ -369,17 +368,22 @@ __global__ void __launch_bounds__(kDecodeThreads)
     if (kRope && jj == jnew) return vrow + slice * 8;
     return vb0 + (size_t)jj * HD;
   };
-  for (int ja = grp; ja < n; ja += 2 * kGroups) {
-    const int jb = ja + kGroups;
-    const uint4 a = *reinterpret_cast<const uint4*>(vrow_ptr(ja));
-    const uint4 b = jb < n ? *reinterpret_cast<const uint4*>(vrow_ptr(jb)) : make_uint4(0, 0, 0, 0);
-    const float pa = sc[ja];
-    const float pb = jb < n ? sc[jb] : 0.f;
-    float ta[8], tb[8];
-    unpack8(a, ta);
-    unpack8(b, tb);
+  for (int j0g = grp; j0g < n; j0g += kUnroll * kGroups) {
+    uint4 vv[kUnroll];
+    float pv[kUnroll];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = fmaf(pb, tb[e], fmaf(pa, ta[e], acc[e]));
+    for (int t = 0; t < kUnroll; ++t) {
+      const int jj = j0g + t * kGroups;
+      vv[t] = jj < n ? *reinterpret_cast<const uint4*>(vrow_ptr(jj)) : make_uint4(0, 0, 0, 0);
+      pv[t] = jj < n ? sc[jj] : 0.f;
+    }
+#pragma unroll
+    for (int t = 0; t < kUnroll; ++t) {
+      float tv[8];
+      unpack8(vv[t], tv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(pv[t], tv[e], acc[e]);
+    }
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) gacc[grp * HD + slice * 8 + e] = acc[e];

@@ -864,18 +864,17 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
     }
   }
   if (!found) return fail(GDSQ_ERR_UNSUPPORTED, "no MoE launch plan fits shared memory");
-  // As for the plain GEMV: when the chosen plan needs more than one wave of
-  // CTAs, a one-stage ring with at least 4 chunks per warp that holds every
-  // item at once is faster (config 4 gate/up at batch 1: 316.6 vs 303.8
-  // tok/s; at batch 8 no such plan fits and the model's choice stays).
+  // As for the plain GEMV: a one-stage ring is faster when it holds every
+  // item in one wave of at least 4 CTAs per SM with at least 4 chunks per
+  // warp (config 4 gate/up at batch 1: 316.6 vs 303.8 tok/s).  At batch 8
+  // no such plan fits, and the down stage at batch 1 (128 items) has too
+  // few CTAs; the model's choice stays there.
   if (!forced) {
-    int occ_pick = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pick, kernel, kGemvWarps * 32, out->smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if ((long long)items * out->cs > (long long)dev.sms * occ_pick) {
-      for (int cs = 1; cs <= out->cs; cs *= 2) {
+    cudaError_t e = cudaSuccess;
+    {
+      for (int cs = 1; cs <= kMaxCluster && cs <= C; cs *= 2) {
         const int mw = ((C + cs - 1) / cs + kGemvWarps - 1) / kGemvWarps;
-        if (mw < 4) continue;
+        if (mw < 4 || (long long)items * cs < 4LL * dev.sms) continue;
         const MoeSmemLayout L1 = moe_smem_layout(C, GS, cs, 1);
         if (L1.total > dev.smem_optin) continue;
         e = ensure_smem(kernel, L1.total, dev.ordinal);
