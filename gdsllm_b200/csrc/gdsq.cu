@@ -1500,8 +1500,9 @@ int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* 
 int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, const void* const* bufs, void* epochs,
                              int cap, int rank, int world, void* stream_v) {
   t_last_error.clear();
-  if (elem_type != GDSQ_ELEM_F16 && elem_type != GDSQ_ELEM_F32)
-    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: elem_type %d is neither fp16 nor fp32", elem_type);
+  if (elem_type != GDSQ_ELEM_F16 && elem_type != GDSQ_ELEM_F32 && elem_type != GDSQ_ELEM_F32_TO_F16)
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: elem_type %d is not fp16, fp32 or fp32 -> fp16",
+                elem_type);
   if (world < 1 || world > kP2PMaxRanks || rank < 0 || rank >= world)
     return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: rank %d of world %d (at most %d ranks)", rank, world,
                 kP2PMaxRanks);
@@ -1510,8 +1511,9 @@ int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, co
                 kLLMaxCtas * kLLElemsPerCta);
   if (n == 0) return GDSQ_OK;
   if (!in || !out || !bufs || !epochs) return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: null pointer");
-  const int esz = elem_type == GDSQ_ELEM_F32 ? 4 : 2;
-  if (!aligned(in, esz) || !aligned(out, esz) || !aligned(epochs, 4))
+  const int esz = elem_type == GDSQ_ELEM_F16 ? 2 : 4;
+  const int osz = elem_type == GDSQ_ELEM_F32 ? 4 : 2;
+  if (!aligned(in, esz) || !aligned(out, osz) || !aligned(epochs, 4))
     return fail(GDSQ_ERR_MISALIGNED, "allreduce words: input, output or epochs misaligned");
   LLArgs a = {};
   for (int r = 0; r < world; ++r) {
@@ -1530,11 +1532,14 @@ int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, co
   a.wait_ns = g_peer_wait_ns.load();
   const int grid = (n + kLLElemsPerCta - 1) / kLLElemsPerCta;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  cudaError_t e = elem_type == GDSQ_ELEM_F32
-                      ? launch(allreduce_ll_kernel<float>, dim3(grid), dim3(kLLThreads), 0, stream,
-                               g_pdl_enabled != 0, a)
-                      : launch(allreduce_ll_kernel<__half>, dim3(grid), dim3(kLLThreads), 0, stream,
-                               g_pdl_enabled != 0, a);
+  cudaError_t e;
+  if (elem_type == GDSQ_ELEM_F32)
+    e = launch(allreduce_ll_kernel<float>, dim3(grid), dim3(kLLThreads), 0, stream, g_pdl_enabled != 0, a);
+  else if (elem_type == GDSQ_ELEM_F16)
+    e = launch(allreduce_ll_kernel<__half>, dim3(grid), dim3(kLLThreads), 0, stream, g_pdl_enabled != 0, a);
+  else
+    e = launch(allreduce_ll_kernel<float, __half, true>, dim3(grid), dim3(kLLThreads), 0, stream,
+               g_pdl_enabled != 0, a);
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "allreduce words launch");
 }
 

@@ -162,7 +162,9 @@ __device__ __forceinline__ void ll_store(T* p, float v) {
   else *p = __float2half_rn(v);
 }
 
-template <typename T>
+// TOut = __half with kClamp: the fp32 sum clamped to the fp16 range, then
+// rounded (a NaN stays a NaN), as y.clamp(-65504, 65504).half().
+template <typename T, typename TOut = T, bool kClamp = false>
 __global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const LLArgs a) {
   __shared__ int s_fail;
   const int c = blockIdx.x;
@@ -217,11 +219,13 @@ __global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const LLArgs a
   if (!ok) s_fail = 1;
   __syncthreads();
   if (s_fail == 0) {
-    T* out = static_cast<T*>(a.out);
+    TOut* out = static_cast<TOut*>(a.out);
 #pragma unroll
     for (int j = 0; j < kLLPerThread; ++j) {
       const int i = base + j * kLLThreads;
-      if (i < a.n) ll_store(out + i, sum[j]);
+      float v = sum[j];
+      if constexpr (kClamp) v = v > 65504.f ? 65504.f : (v < -65504.f ? -65504.f : v);
+      if (i < a.n) ll_store(out + i, v);
     }
   }
   if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(a.epochs + c) = e;

@@ -65,6 +65,10 @@ class ExpertParallelMoE:
         ids, weights, sw = self.router(x2d, self.layer.router, self.top_k, sg)
         y32 = self.partial(x2d, ids, weights, self.layer, out=out32, include_shared=self.rank == 0,
                            shared_weights=sw)
+        if self.allreduce is not None and getattr(self.allreduce, "finishes_fp16", False):
+            y = torch.empty(y32.shape, dtype=x.dtype, device=y32.device)
+            self.allreduce(y32, out=y)  # sum, clamp and fp16 in the exchange kernel
+            return y.view(x.shape)
         if self.allreduce is not None:
             self.allreduce(y32)
         else:

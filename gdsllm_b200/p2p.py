@@ -109,11 +109,20 @@ class PeerWordAllReduce:
         self.peer = PeerBuffers(2 * world * self.cap * 8, WORDS_EPOCHS, group, device)
         self.rank, self.world = self.peer.rank, self.peer.world
 
+    # fp32 in, fp16 out (the sum clamped to the fp16 range) in one kernel
+    finishes_fp16 = True
+
     def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Sum of ``t`` (fp16 or fp32, contiguous) over the ranks; in place
-        unless ``out`` is given."""
+        unless ``out`` is given.  fp32 ``t`` with an fp16 ``out`` gives the
+        sum clamped to +-65504 and rounded to fp16 (``moe.finish``)."""
         out = t if out is None else out
-        kind = {torch.float16: 0, torch.float32: 1}[t.dtype]
+        if t.dtype == torch.float32 and out.dtype == torch.float16:
+            kind = 2
+        else:
+            if out.dtype != t.dtype:
+                raise ValueError(f"allreduce words: {t.dtype} in, {out.dtype} out")
+            kind = {torch.float16: 0, torch.float32: 1}[t.dtype]
         stream = torch.cuda.current_stream(t.device).cuda_stream
         check(lib().gdsq_allreduce_sum_words(kind, t.data_ptr(), out.data_ptr(), t.numel(), self.peer.bufs,
                                              self.peer.flags_t.data_ptr(), self.cap, self.rank, self.world, stream),

@@ -228,9 +228,11 @@ GDSQ_API int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void
 
 #define GDSQ_ELEM_F16 0
 #define GDSQ_ELEM_F32 1
+#define GDSQ_ELEM_F32_TO_F16 2 /* fp32 in; out fp16 of the sum clamped to +-65504 (qwen_moe.py:514) */
 
 /* out[i] = sum over ranks r (in rank order, fp32) of in_r[i], fp16 or fp32
- * (elem_type GDSQ_ELEM_F16 / GDSQ_ELEM_F32), over NVLink peer memory: every
+ * (elem_type GDSQ_ELEM_F16 / GDSQ_ELEM_F32; GDSQ_ELEM_F32_TO_F16 adds fp32
+ * and writes the clamped fp16 result), over NVLink peer memory: every
  * rank stores each element with the call's epoch as one 64-bit word into
  * every rank's buffer and waits only on its own buffer (no flags).  The
  * expert-parallel exchange of the MoE partial sums (no reference

@@ -67,6 +67,15 @@ def _worker(rank, world, port, q):
             dist.all_reduce(ref)
             out = words(t.clone())
             worst_w = max(worst_w, ((out.float() - ref).abs() / (ref.abs() + 1)).max().item())
+        # fp32 partials in, the clamped fp16 sum out (moe.finish in the same kernel)
+        t = (3e4 * torch.randn(8 * hidden, generator=torch.Generator().manual_seed(250 + rank))).to(dev)
+        ref = t.clone()
+        dist.all_reduce(ref)
+        out16 = torch.empty(8 * hidden, dtype=torch.float16, device=dev)
+        words(t, out=out16)
+        ref16 = ref.clamp(min=-65504.0, max=65504.0).half()
+        res["words_f16_equal"] = torch.equal(out16, ref16)
+        res["words_f16_diff"] = ((out16.float() - ref16.float()).abs() / (ref16.float().abs() + 1)).max().item()
         gin = torch.empty(8 * hidden, dtype=torch.float32, device=dev)
         s0 = torch.cuda.Stream()
         s0.wait_stream(torch.cuda.current_stream())
@@ -244,6 +253,7 @@ def test_expert_and_tensor_parallel_on_gpus(world):
         # two ranks: NCCL adds a + b as the word all-reduce does (same bits);
         # more ranks: NCCL's order may differ, one fp16 rounding apart
         assert res["ep_words_equal"] or (world > 2 and res["ep_words_diff"] <= 2e-3 * res["ep_scale"] + 1e-3), (rank, res)
+        assert res["words_f16_equal"] or (world > 2 and res["words_f16_diff"] <= 2e-3), (rank, res)
         assert res["words"] <= 1e-3, (rank, res)   # fp32 rank-order sum vs NCCL (fp16 inputs summed in fp32)
         assert res["words_err"] == 0, (rank, res)
         # fused row split: fp32 partials summed in rank order then one fp16
