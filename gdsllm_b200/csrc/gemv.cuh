@@ -470,15 +470,18 @@ __device__ __forceinline__ void stage_x_affine(const __half* __restrict__ x, uin
 // between batch rows; `xc` / `xcb` likewise for the per-block offset terms
 // (GGUF formats).  acc[] accumulates in units of 2^-39.
 
-template <int B>
-__device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t xb, uint32_t xc,
-                                           uint32_t xcb, float (&acc)[B]) {
-  uint32_t w[36];
+// This lane's row of a Q4_0 chunk (8 blocks, 144 bytes) into registers.
+__device__ __forceinline__ void load_chunk_q4_0(uint32_t src, uint32_t (&w)[36]) {
 #pragma unroll
   for (int j = 0; j < 9; ++j) {
     const uint4 v = lds128(src + 16 * j);
     w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
   }
+}
+
+template <int B>
+__device__ __forceinline__ void chunk_q4_0_regs(const uint32_t (&w)[36], uint32_t xa, uint32_t xb, uint32_t xc,
+                                                uint32_t xcb, float (&acc)[B]) {
 #pragma unroll
   for (int blk = 0; blk < 8; ++blk) {
     const int o = 18 * blk;  // byte offset of the block inside the chunk
@@ -516,6 +519,14 @@ __device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t x
       acc[b] = fmaf(d, sum, acc[b]);
     }
   }
+}
+
+template <int B>
+__device__ __forceinline__ void chunk_q4_0(uint32_t src, uint32_t xa, uint32_t xb, uint32_t xc,
+                                           uint32_t xcb, float (&acc)[B]) {
+  uint32_t w[36];
+  load_chunk_q4_0(src, w);
+  chunk_q4_0_regs<B>(w, xa, xb, xc, xcb, acc);
 }
 
 template <int B>
@@ -576,16 +587,21 @@ __device__ __forceinline__ void chunk_q8_0(uint32_t src, uint32_t xa, uint32_t x
 // group, both sums fp32.  `sb_row` (shared address of this lane's (scale,
 // bias) row) and `xsum` are indexed by the group's position in the K slice,
 // starting at g0.
-template <int B, int GS>
-__device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_t xa, uint32_t xb,
-                                             uint32_t xsum, uint32_t xsum_b, uint32_t sb_row,
-                                             int g0, float (&acc)[B]) {
-  uint32_t w[32];
+
+
+// This lane's row of an affine chunk (32 words, a 128-byte swizzled box row)
+// into registers.
+__device__ __forceinline__ void load_chunk_affine(uint32_t src, uint32_t swz, uint32_t (&w)[32]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint4 v = lds128(src + 16 * (j ^ swz));  // 128-byte swizzled box row
+    const uint4 v = lds128(src + 16 * (j ^ swz));
     w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
   }
+}
+
+template <int B, int GS>
+__device__ __forceinline__ void chunk_affine_regs(const uint32_t (&w)[32], uint32_t xa, uint32_t xb, uint32_t xsum,
+                                                  uint32_t xsum_b, uint32_t sb_row, int g0, float (&acc)[B]) {
   constexpr int kGroupsPerChunk = kChunkCols / GS;
   constexpr int kWordsPerGroup = GS / 8;
 #pragma unroll
@@ -615,6 +631,15 @@ __device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_
       acc[b] = fmaf(sbf.x, (s0[b].x + s0[b].y) + (s1[b].x + s1[b].y),
                     fmaf(sbf.y, lds32f(xsum + b * xsum_b + 4 * g), acc[b]));
   }
+}
+
+template <int B, int GS>
+__device__ __forceinline__ void chunk_affine(uint32_t src, uint32_t swz, uint32_t xa, uint32_t xb,
+                                             uint32_t xsum, uint32_t xsum_b, uint32_t sb_row,
+                                             int g0, float (&acc)[B]) {
+  uint32_t w[32];
+  load_chunk_affine(src, swz, w);
+  chunk_affine_regs<B, GS>(w, xa, xb, xsum, xsum_b, sb_row, g0, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -821,6 +846,29 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
         fail_pending = issued - consumed;  // copies issued and not yet consumed
       }
       ++consumed;
+      if (F == kFmtQ4_0 && CP == 1) {
+        // One chunk per stage: the lane's row goes to registers first, and
+        // the stage is refilled before the arithmetic, so the next copy
+        // overlaps it (an extra stage of buffering in registers).
+        if (ok) {
+          const uint32_t slot = ring_a + stage * stage_bytes<F>(1);
+          const int cl = wc0 + st;
+          uint32_t w[36];
+          load_chunk_q4_0(slot, w);
+          __syncwarp();
+          if (issued < total) {
+            if (lane == 0) fence_proxy_async_smem();  // the reads above before the copy's writes
+            issue_next();
+          }
+          chunk_q4_0_regs<B>(w, xs_a + cl * (kChunkCols * 4), xb, xsum_a + cl * 32, (ld / 32) * 4, acc);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+        continue;
+      }
       if (ok) {
         const uint32_t slot = ring_a + stage * stage_bytes<F>(CP);
         const int cl0 = wc0 + st * CP;  // slice-local chunk
