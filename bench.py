@@ -997,10 +997,10 @@ def bench_config4(args, dist):
 
     def step(stream):
         x = x0
-        for l in range(NL):
+        for l in range(NL):  # x + moe(x), the residual add inside the layer's last launch
             layer = layers[l % NPHYS]
-            y = mods[l % NPHYS](x) if ws > 1 else moe.moe_mlp_decode(x, layer, TOPK)
-            x = x + y
+            x = (mods[l % NPHYS](x, add_residual=True) if ws > 1
+                 else moe.moe_mlp_decode(x, layer, TOPK, add_residual=True))
         return x
 
     # bytes touched per step (whole job): routing of an eager pass
@@ -1012,7 +1012,8 @@ def bench_config4(args, dist):
             ids = moe.route(x, layer.router, TOPK)[0]
             distinct = int(torch.unique(ids).numel())
             touched += E * H * 2 + (distinct + 1) * 3 * (I * H // 2 + 2 * 2 * I * H // G)
-            x = x + (mods[l % NPHYS](x) if ws > 1 else moe.moe_mlp_decode(x, layer, TOPK))
+            x = (mods[l % NPHYS](x, add_residual=True) if ws > 1
+                 else moe.moe_mlp_decode(x, layer, TOPK, add_residual=True))
     torch.cuda.synchronize()
     g = capture(step)
     ms, clk = time_graph(g, args.steps, args.warmup, dist, dist.clocks)
@@ -1035,7 +1036,8 @@ def bench_config4(args, dist):
             "roofline": {"bound": "hbm", "achieved": round(touched / ws / step_s / 1e9, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(touched / ws / step_s / 1e9 / peak, 4), "peak_kind": peak_kind,
                          "scope": "touched weight bytes per GPU / step time (whole step)"},
-            "gpu_launches": args.steps * NL * (4 + 4), "clocks": clk}
+            # this build's kernels per layer: route, gate/up, down (+ the word exchange over ranks)
+            "gpu_launches": args.steps * NL * (3 + (1 if exch is not None else 0)), "clocks": clk}
 
 
 def main():

@@ -62,6 +62,12 @@ _C_SIGNATURES = {
                                   [ctypes.c_float, ctypes.c_void_p]),
     "gdsq_attention_decode_rope_f16": (ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4 +
                                        [ctypes.c_float, ctypes.c_void_p]),
+    "gdsq_allreduce_sum_words_residual": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                                         ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                         ctypes.c_void_p, ctypes.c_void_p]),
+    "gdsq_moe_affine_q4_down_residual": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_void_p] * 5 +
+                                         [ctypes.c_int] * 9 + [ctypes.c_void_p, ctypes.c_void_p]),
     "gdsq_silu_mul_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                          ctypes.c_void_p]),
     "gdsq_argmax_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,

@@ -786,7 +786,8 @@ torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, 
                                      int64_t expert_first, int64_t expert_total,
                                      c10::optional<torch::Tensor> out, bool accumulate, bool out_fp32,
                                      c10::optional<torch::Tensor> h, c10::optional<std::vector<torch::Tensor>> shared,
-                                     c10::optional<torch::Tensor> shared_weights, bool clamp) {
+                                     c10::optional<torch::Tensor> shared_weights, bool clamp,
+                                     c10::optional<torch::Tensor> residual) {
   const char* op = "fused_moe_affine_q4";
   if (!x.is_cuda() || x.scalar_type() != torch::kFloat16)
     throw std::runtime_error("fused_moe_affine_q4: x must be a CUDA float16 tensor");
@@ -871,6 +872,21 @@ torch::Tensor py_fused_moe_affine_q4(torch::Tensor x, torch::Tensor expert_ids, 
   raise_status(st, op);
   const int flags = (out_fp32 ? GDSQ_MOE_OUT_F32 : 0) | (accumulate ? GDSQ_MOE_ACCUMULATE : 0) |
                     (clamp ? GDSQ_MOE_CLAMP : 0);
+  if (residual.has_value()) {
+    const torch::Tensor& r = *residual;
+    if (out_fp32 || accumulate || !r.is_cuda() || r.device() != dev || r.scalar_type() != torch::kFloat16 ||
+        !r.is_contiguous() || r.numel() != ntok * hidden)
+      throw std::runtime_error("fused_moe_affine_q4: residual must be a contiguous float16 CUDA tensor shaped like "
+                               "x, with an fp16 output that does not accumulate");
+    st = gdsq_moe_affine_q4_down_residual(
+        std::get<0>(down).data_ptr(), std::get<1>(down).data_ptr(), std::get<2>(down).data_ptr(), sh[6], sh[7],
+        sh[8], hb.data_ptr(), ids.data_ptr<int32_t>(), rw.data_ptr(), has_shared ? sw.data_ptr() : nullptr,
+        y.data_ptr(), static_cast<int>(ntok), static_cast<int>(top_k), static_cast<int>(hidden),
+        static_cast<int>(inter), group_size, static_cast<int>(expert_first), static_cast<int>(experts),
+        static_cast<int>(expert_total), flags, r.data_ptr(), stream);
+    raise_status(st, op);
+    return y;
+  }
   st = gdsq_moe_affine_q4_down(std::get<0>(down).data_ptr(), std::get<1>(down).data_ptr(),
                                std::get<2>(down).data_ptr(), sh[6], sh[7], sh[8], hb.data_ptr(),
                                ids.data_ptr<int32_t>(), rw.data_ptr(), has_shared ? sw.data_ptr() : nullptr,
@@ -994,7 +1010,7 @@ PYBIND11_MODULE(gds_io_ext, m) {
         py::arg("down"), py::arg("group_size") = 128, py::arg("expert_first") = 0, py::arg("expert_total") = -1,
         py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("out_fp32") = false,
         py::arg("h") = py::none(), py::arg("shared") = py::none(), py::arg("shared_weights") = py::none(),
-        py::arg("clamp") = false);
+        py::arg("clamp") = false, py::arg("residual") = py::none());
   m.def("moe_route", &py_moe_route,
         "Top-k expert ids, softmax weights and the shared expert's sigmoid gate from router logits (one launch).",
         py::arg("logits"), py::arg("top_k"), py::arg("x") = py::none(), py::arg("shared_gate") = py::none());

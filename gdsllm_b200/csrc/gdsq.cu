@@ -977,9 +977,12 @@ int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, cons
                  const void* shw1, const void* shs1, const void* shb1, const void* shared_route,
                  const void* x, const int32_t* ids, const void* route, void* out, int ntok, int top_k,
                  int rows, int cols, int group, int e_first, int e_count, int e_total, int flags,
-                 void* stream_v) {
+                 void* stream_v, const void* residual = nullptr) {
   t_last_error.clear();
   const char* name = stage == 0 ? "moe gate/up" : "moe down";
+  if (residual && (stage != 1 || (flags & (kMoeOutF32 | kMoeAccumulate)) || !aligned(residual, 2)))
+    return fail(GDSQ_ERR_INVALID_VALUE, "%s: a residual needs the down stage's fp16 output without "
+                "accumulation, 2-byte aligned", name);
   // The shared expert is present when all of its pointers are given.
   const void* sh_ptrs[7] = {shw0, shs0, shb0, shw1, shs1, shb1, shared_route};
   const int n_sh = stage == 0 ? 6 : 3;
@@ -1045,6 +1048,7 @@ int moe_dispatch(int stage, const void* w0, const void* s0, const void* b0, cons
   p.rows = rows;
   p.K = cols;
   p.flags = stage == 1 ? flags : 0;
+  p.residual = static_cast<const __half*>(residual);
   p.w0 = static_cast<const uint32_t*>(w0);
   p.w1 = static_cast<const uint32_t*>(w1);
   p.group = group;
@@ -1370,6 +1374,23 @@ int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_scales, co
                       expert_first, expert_count, expert_total, flags, stream);
 }
 
+int gdsq_moe_affine_q4_down_residual(const void* down_weight, const void* down_scales, const void* down_biases,
+                                     const void* shared_down_weight, const void* shared_down_scales,
+                                     const void* shared_down_biases, const void* h, const int32_t* expert_ids,
+                                     const void* route_weights, const void* shared_weights, void* y,
+                                     int num_tokens, int top_k, int hidden_dim, int inter_dim, int group_size,
+                                     int expert_first, int expert_count, int expert_total, int flags,
+                                     const void* residual, void* stream) {
+  if (!residual) {
+    t_last_error.clear();
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe down: null residual");
+  }
+  return moe_dispatch(1, down_weight, down_scales, down_biases, nullptr, nullptr, nullptr, shared_down_weight,
+                      shared_down_scales, shared_down_biases, nullptr, nullptr, nullptr, shared_weights, h,
+                      expert_ids, route_weights, y, num_tokens, top_k, hidden_dim, inter_dim, group_size,
+                      expert_first, expert_count, expert_total, flags, stream, residual);
+}
+
 }  // extern "C"
 
 namespace gdsq {
@@ -1499,7 +1520,17 @@ int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void* const* 
 
 int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, const void* const* bufs, void* epochs,
                              int cap, int rank, int world, void* stream_v) {
+  return gdsq_allreduce_sum_words_residual(elem_type, in, out, n, bufs, epochs, cap, rank, world, nullptr,
+                                           stream_v);
+}
+
+int gdsq_allreduce_sum_words_residual(int elem_type, const void* in, void* out, int n, const void* const* bufs,
+                                      void* epochs, int cap, int rank, int world, const void* residual,
+                                      void* stream_v) {
   t_last_error.clear();
+  if (residual && (elem_type != GDSQ_ELEM_F32_TO_F16 || !aligned(residual, 2)))
+    return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: a residual needs GDSQ_ELEM_F32_TO_F16 and 2-byte "
+                "alignment");
   if (elem_type != GDSQ_ELEM_F16 && elem_type != GDSQ_ELEM_F32 && elem_type != GDSQ_ELEM_F32_TO_F16)
     return fail(GDSQ_ERR_INVALID_VALUE, "allreduce words: elem_type %d is not fp16, fp32 or fp32 -> fp16",
                 elem_type);
@@ -1530,6 +1561,7 @@ int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, co
   a.rank = rank;
   a.world = world;
   a.wait_ns = g_peer_wait_ns.load();
+  a.residual = static_cast<const __half*>(residual);
   const int grid = (n + kLLElemsPerCta - 1) / kLLElemsPerCta;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   cudaError_t e;

@@ -77,6 +77,9 @@ struct MoeParams {
   const __half* ss1;    // matrix 1 (stage 0)
   const __half* sb1;
   const __half* shared_route;  // [ntok] fp16 weight of the shared slot (stage 1)
+  // Stage 1, fp16 output: y = residual + fp16(result) in fp16 (the caller's
+  // `x + moe(x)`, qwen_moe.py's residual add, in the same two roundings).
+  const __half* residual;
   // Generic kernels only: packed words of the matrices (the fast kernels
   // read them through tensor maps).
   const uint32_t* w0;
@@ -410,7 +413,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
             y[o] = moe_finish((p.flags & kMoeAccumulate) ? y[o] + v : v, p.flags);
           } else {
             __half* y = static_cast<__half*>(p.out);
-            y[o] = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + v : v, p.flags));
+            const __half r = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + v : v,
+                                                        p.flags));
+            y[o] = p.residual ? __hadd(p.residual[o], r) : r;
           }
         }
       }
@@ -509,7 +514,9 @@ __global__ void __launch_bounds__(256) moe_down_generic_kernel(const MoeParams p
       y[o] = moe_finish((p.flags & kMoeAccumulate) ? y[o] + acc : acc, p.flags);
     } else {
       __half* y = static_cast<__half*>(p.out);
-      y[o] = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + acc : acc, p.flags));
+      const __half r = __float2half_rn(moe_finish((p.flags & kMoeAccumulate) ? __half2float(y[o]) + acc : acc,
+                                                  p.flags));
+      y[o] = p.residual ? __hadd(p.residual[o], r) : r;
     }
   }
 }

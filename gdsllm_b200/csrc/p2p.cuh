@@ -148,6 +148,7 @@ struct LLArgs {
   int rank;
   int world;
   unsigned long long wait_ns;              // bound of the wait for the peers' words
+  const __half* residual;                  // fp32 -> fp16 form: out = residual + fp16(sum) in fp16, or null
 };
 
 template <typename T>
@@ -225,7 +226,14 @@ __global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const LLArgs a
       const int i = base + j * kLLThreads;
       float v = sum[j];
       if constexpr (kClamp) v = v > 65504.f ? 65504.f : (v < -65504.f ? -65504.f : v);
-      if (i < a.n) ll_store(out + i, v);
+      if constexpr (kClamp) {
+        if (i < a.n) {
+          const __half r = __float2half_rn(v);
+          out[i] = a.residual ? __hadd(a.residual[i], r) : r;
+        }
+      } else if (i < a.n) {
+        ll_store(out + i, v);
+      }
     }
   }
   if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(a.epochs + c) = e;

@@ -59,7 +59,10 @@ class ExpertParallelMoE:
         self.router = router or moe.route
         self.allreduce = allreduce  # in-place sum of the fp32 partial; None -> NCCL
 
-    def forward(self, x: torch.Tensor, out32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out32: Optional[torch.Tensor] = None,
+                add_residual: bool = False) -> torch.Tensor:
+        """The layer's output, or x + output (the caller's residual add in
+        the same fp16 roundings) with ``add_residual``."""
         x2d = x.reshape(-1, x.shape[-1])
         sg = self.layer.shared_gate if self.layer.shared is not None else None
         ids, weights, sw = self.router(x2d, self.layer.router, self.top_k, sg)
@@ -67,12 +70,14 @@ class ExpertParallelMoE:
                            shared_weights=sw)
         if self.allreduce is not None and getattr(self.allreduce, "finishes_fp16", False):
             y = torch.empty(y32.shape, dtype=x.dtype, device=y32.device)
-            self.allreduce(y32, out=y)  # sum, clamp and fp16 in the exchange kernel
+            # sum, clamp, fp16 (and the residual add) in the exchange kernel
+            self.allreduce(y32, out=y, residual=x2d.contiguous() if add_residual else None)
             return y.view(x.shape)
         if self.allreduce is not None:
             self.allreduce(y32)
         else:
             dist.all_reduce(y32, op=dist.ReduceOp.SUM, group=self.group)
-        return moe.finish(y32, x)
+        y = moe.finish(y32, x)
+        return x + y if add_residual else y
 
     __call__ = forward

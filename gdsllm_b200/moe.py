@@ -91,7 +91,7 @@ def _shared_list(layer: "MoeLayer"):
 def moe_partial(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer: MoeLayer,
                 out: Optional[torch.Tensor] = None, include_shared: bool = True,
                 shared_weights: Optional[torch.Tensor] = None, out_fp32: bool = True,
-                clamp: bool = False) -> torch.Tensor:
+                clamp: bool = False, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """[B, hidden]: sum over this device's resident routed experts, plus the
     shared expert (weighted by ``shared_weights``) when ``include_shared`` --
     one gate/up launch and one down launch.  fp32 by default (partial sums
@@ -105,7 +105,8 @@ def moe_partial(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, lay
     _ext().fused_moe_affine_q4(x2d, ids, weights, layer.gate, layer.up, layer.down, group_size=layer.group,
                                expert_first=layer.expert_first, expert_total=layer.total, out=out,
                                out_fp32=out_fp32, shared=_shared_list(layer) if use_shared else None,
-                               shared_weights=shared_weights if use_shared else None, clamp=clamp)
+                               shared_weights=shared_weights if use_shared else None, clamp=clamp,
+                               residual=residual)
     return out
 
 
@@ -114,10 +115,13 @@ def finish(y32: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
     return y32.clamp(min=-65504.0, max=65504.0).to(like.dtype).view(like.shape)
 
 
-def moe_mlp_decode(x: torch.Tensor, layer: MoeLayer, top_k: int = 10) -> torch.Tensor:
+def moe_mlp_decode(x: torch.Tensor, layer: MoeLayer, top_k: int = 10, add_residual: bool = False) -> torch.Tensor:
     """One MoE MLP on one GPU: x (B, S, hidden) or (B, hidden) fp16.  Three
-    launches after the router's F.linear: route, gate/up, down (clamped fp16)."""
+    launches after the router's F.linear: route, gate/up, down (clamped fp16).
+    ``add_residual`` returns x + moe(x) (the caller's residual add, in the
+    same fp16 roundings) from the down launch itself."""
     x2d = x.reshape(-1, x.shape[-1])
     ids, weights, sw = route(x2d, layer.router, top_k, layer.shared_gate if layer.shared is not None else None)
-    y = moe_partial(x2d, ids, weights, layer, shared_weights=sw, out_fp32=False, clamp=True)
+    y = moe_partial(x2d, ids, weights, layer, shared_weights=sw, out_fp32=False, clamp=True,
+                    residual=x2d.contiguous() if add_residual else None)
     return y.view(x.shape)

@@ -112,10 +112,12 @@ class PeerWordAllReduce:
     # fp32 in, fp16 out (the sum clamped to the fp16 range) in one kernel
     finishes_fp16 = True
 
-    def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Sum of ``t`` (fp16 or fp32, contiguous) over the ranks; in place
         unless ``out`` is given.  fp32 ``t`` with an fp16 ``out`` gives the
-        sum clamped to +-65504 and rounded to fp16 (``moe.finish``)."""
+        sum clamped to +-65504 and rounded to fp16 (``moe.finish``), plus
+        ``residual`` (fp16) in fp16 when given."""
         out = t if out is None else out
         if t.dtype == torch.float32 and out.dtype == torch.float16:
             kind = 2
@@ -123,10 +125,14 @@ class PeerWordAllReduce:
             if out.dtype != t.dtype:
                 raise ValueError(f"allreduce words: {t.dtype} in, {out.dtype} out")
             kind = {torch.float16: 0, torch.float32: 1}[t.dtype]
+        if residual is not None and (kind != 2 or residual.dtype != torch.float16 or
+                                     residual.numel() != t.numel()):
+            raise ValueError("allreduce words: a residual needs fp32 in, fp16 out and fp16 residual of the same size")
         stream = torch.cuda.current_stream(t.device).cuda_stream
-        check(lib().gdsq_allreduce_sum_words(kind, t.data_ptr(), out.data_ptr(), t.numel(), self.peer.bufs,
-                                             self.peer.flags_t.data_ptr(), self.cap, self.rank, self.world, stream),
-              "gdsq_allreduce_sum_words")
+        check(lib().gdsq_allreduce_sum_words_residual(kind, t.data_ptr(), out.data_ptr(), t.numel(), self.peer.bufs,
+                                                      self.peer.flags_t.data_ptr(), self.cap, self.rank, self.world,
+                                                      None if residual is None else residual.data_ptr(), stream),
+              "gdsq_allreduce_sum_words_residual")
         return out
 
     def close(self):

@@ -185,6 +185,19 @@ GDSQ_API int gdsq_moe_affine_q4_down(const void* down_weight, const void* down_s
                                      int hidden_dim, int inter_dim, int group_size, int expert_first,
                                      int expert_count, int expert_total, int flags, void* stream);
 
+/* gdsq_moe_affine_q4_down with fp16 y = residual + fp16(result), added in
+ * fp16 (the caller's `x + moe(x)` residual add in the same two roundings;
+ * residual fp16 [num_tokens][hidden_dim], may be y itself).  flags may not
+ * hold GDSQ_MOE_OUT_F32 or GDSQ_MOE_ACCUMULATE. */
+GDSQ_API int gdsq_moe_affine_q4_down_residual(const void* down_weight, const void* down_scales,
+                                              const void* down_biases, const void* shared_down_weight,
+                                              const void* shared_down_scales, const void* shared_down_biases,
+                                              const void* h, const int32_t* expert_ids, const void* route_weights,
+                                              const void* shared_weights, void* y, int num_tokens, int top_k,
+                                              int hidden_dim, int inter_dim, int group_size, int expert_first,
+                                              int expert_count, int expert_total, int flags, const void* residual,
+                                              void* stream);
+
 /* gdsq_moe_affine_q4_gate_up then gdsq_moe_affine_q4_down (same arguments,
  * same results) with the intermediate h kept in a fixed 4 MiB array of the
  * library's static device memory instead of a caller buffer, so the call
@@ -245,6 +258,14 @@ GDSQ_API int gdsq_allreduce_sum_f16(const void* in, void* out, int n, const void
  * output unwritten. */
 GDSQ_API int gdsq_allreduce_sum_words(int elem_type, const void* in, void* out, int n, const void* const* bufs,
                                       void* epochs, int cap, int rank, int world, void* stream);
+
+/* The same with elem_type GDSQ_ELEM_F32_TO_F16 and out = residual + the
+ * clamped fp16 sum, added in fp16 (the caller's `x + moe(x)` of the
+ * expert-parallel layer in the same roundings); residual fp16 [n], may be
+ * out itself. */
+GDSQ_API int gdsq_allreduce_sum_words_residual(int elem_type, const void* in, void* out, int n,
+                                               const void* const* bufs, void* epochs, int cap, int rank, int world,
+                                               const void* residual, void* stream);
 
 /* A row-split (K-sharded) Q4_0 / Q8_0 GEMV whose output rows are summed over
  * the tensor-parallel ranks inside the kernel: y = sum over ranks r of

@@ -275,6 +275,12 @@ def test_moe_layer_decode_matches_reference_layer(cuda):
     assert np.isfinite(got).all()
     assert (err <= tol).all(), f"worst err/bar {(err / tol).max():.3f}"
     assert idn.shape == (1, top_k + 1)
+    # the residual add inside the down launch: the bits of x + moe(x) in fp16
+    xd = x.to(cuda)
+    xr = moe.moe_mlp_decode(xd, layer, top_k, add_residual=True)
+    assert torch.equal(xr, xd + y)
+    with pytest.raises(RuntimeError, match="residual"):
+        moe.moe_partial(xd.view(1, hidden), ids, w, layer, out_fp32=True, residual=xd.view(1, hidden))
 
 
 @pytest.mark.parametrize("ntok,top_k", [(1, 10), (8, 10), (3, 4)])

@@ -59,6 +59,9 @@ def _worker(rank, world, port, q):
         y_ep_words = ep.ExpertParallelMoE(local, top_k=10, allreduce=words)(x)
         res["ep_words_equal"] = torch.equal(y_ep_words, y_ep)
         res["ep_words_diff"] = (y_ep_words.float() - y_ep.float()).abs().max().item()
+        # the residual add inside the exchange kernel: x + layer(x) in fp16
+        y_res = ep.ExpertParallelMoE(local, top_k=10, allreduce=words)(x, add_residual=True)
+        res["ep_residual_equal"] = torch.equal(y_res, x + y_ep_words)
         worst_w = 0.0
         for it, (nel, dt) in enumerate([(8 * hidden, torch.float32), (1000, torch.float32), (4096, torch.float16),
                                         (8 * hidden, torch.float32), (7, torch.float16)]):
@@ -254,6 +257,7 @@ def test_expert_and_tensor_parallel_on_gpus(world):
         # more ranks: NCCL's order may differ, one fp16 rounding apart
         assert res["ep_words_equal"] or (world > 2 and res["ep_words_diff"] <= 2e-3 * res["ep_scale"] + 1e-3), (rank, res)
         assert res["words_f16_equal"] or (world > 2 and res["words_f16_diff"] <= 2e-3), (rank, res)
+        assert res["ep_residual_equal"], (rank, res)
         assert res["words"] <= 1e-3, (rank, res)   # fp32 rank-order sum vs NCCL (fp16 inputs summed in fp32)
         assert res["words_err"] == 0, (rank, res)
         # fused row split: fp32 partials summed in rank order then one fp16
