@@ -1009,7 +1009,7 @@ def bench_config4(args, dist):
     with torch.no_grad():
         for l in range(NL):
             layer = layers[l % NPHYS]
-            ids = moe.route(x, layer.router, TOPK)[0]
+            ids = moe.route_fused(x, layer, TOPK)[0]
             distinct = int(torch.unique(ids).numel())
             touched += E * H * 2 + (distinct + 1) * 3 * (I * H // 2 + 2 * 2 * I * H // G)
             x = (mods[l % NPHYS](x, add_residual=True) if ws > 1
@@ -1036,7 +1036,7 @@ def bench_config4(args, dist):
             "roofline": {"bound": "hbm", "achieved": round(touched / ws / step_s / 1e9, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(touched / ws / step_s / 1e9 / peak, 4), "peak_kind": peak_kind,
                          "scope": "touched weight bytes per GPU / step time (whole step)"},
-            # this build's kernels per layer: route, gate/up, down (+ the word exchange over ranks)
+            # this build's kernels per layer: router + route, gate/up, down (+ the word exchange over ranks)
             "gpu_launches": args.steps * NL * (3 + (1 if exch is not None else 0)), "clocks": clk}
 
 

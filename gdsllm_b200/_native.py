@@ -68,6 +68,8 @@ _C_SIGNATURES = {
                                                          ctypes.c_void_p, ctypes.c_void_p]),
     "gdsq_moe_affine_q4_down_residual": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_void_p] * 5 +
                                          [ctypes.c_int] * 9 + [ctypes.c_void_p, ctypes.c_void_p]),
+    "gdsq_moe_router": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 6),
     "gdsq_silu_mul_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                          ctypes.c_void_p]),
     "gdsq_argmax_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,

@@ -1575,6 +1575,43 @@ int gdsq_allreduce_sum_words_residual(int elem_type, const void* in, void* out, 
   return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "allreduce words launch");
 }
 
+int gdsq_moe_router(const void* x, int num_tokens, int hidden_dim, const void* router_weight, int num_experts,
+                    const void* shared_gate, int top_k, void* logits, int32_t* expert_ids, void* route_weights,
+                    void* shared_weights, unsigned int* counter, void* stream_v) {
+  t_last_error.clear();
+  if (num_tokens < 0 || num_tokens > kRouterMaxTokens || num_experts < 1 || num_experts > 32 * kRouteLaneVals ||
+      top_k < 1 || top_k > 32 || top_k > num_experts || hidden_dim <= 0 || hidden_dim % 512 != 0)
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe router: tokens %d (<= %d), experts %d (<= %d), top_k %d (<= 32), "
+                "hidden %d (a multiple of 512)", num_tokens, kRouterMaxTokens, num_experts, 32 * kRouteLaneVals,
+                top_k, hidden_dim);
+  if (num_tokens == 0) return GDSQ_OK;
+  if (!x || !router_weight || !logits || !expert_ids || !route_weights || !counter ||
+      (shared_gate && !shared_weights))
+    return fail(GDSQ_ERR_INVALID_VALUE, "moe router: null pointer");
+  if (!aligned(x, 16) || !aligned(router_weight, 16) || (shared_gate && !aligned(shared_gate, 16)) ||
+      !aligned(logits, 2) || !aligned(expert_ids, 4) || !aligned(route_weights, 2) || !aligned(counter, 4) ||
+      (shared_weights && !aligned(shared_weights, 2)))
+    return fail(GDSQ_ERR_MISALIGNED, "moe router: x and the weights 16-byte, ids and counter 4-byte, "
+                "fp16 outputs 2-byte alignment");
+  const DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st != GDSQ_OK) return st;
+  const int rows = num_experts + (shared_gate ? 1 : 0);
+  const int grid = (rows + kRouterRowsPerCta - 1) / kRouterRowsPerCta;
+  const size_t smem = (size_t)kRouterWarps * (num_experts + 64) * sizeof(float) +
+                      (size_t)kRouterWarps * (num_experts + 8) * sizeof(__half);
+  auto kernel = num_tokens == 1 ? moe_router_kernel<1> : num_tokens <= 4 ? moe_router_kernel<4>
+                                                                          : moe_router_kernel<16>;
+  cudaError_t e = ensure_smem(kernel, (int)smem, dev->ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(moe router)");
+  e = launch(kernel, dim3(grid), dim3(kRouterWarps * 32), smem, static_cast<cudaStream_t>(stream_v),
+             g_pdl_enabled != 0, static_cast<const __half*>(x), num_tokens, hidden_dim,
+             static_cast<const __half*>(router_weight), num_experts, static_cast<const __half*>(shared_gate), top_k,
+             static_cast<__half*>(logits), expert_ids, static_cast<__half*>(route_weights),
+             static_cast<__half*>(shared_weights), counter);
+  return e == cudaSuccess ? GDSQ_OK : cuda_fail(e, "moe router launch");
+}
+
 int gdsq_moe_route(const void* logits, int num_tokens, int num_experts, int top_k, const void* x,
                    const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
                    void* shared_weights, void* stream_v) {

@@ -602,23 +602,17 @@ __device__ __forceinline__ void route_select_sorted(const __half* __restrict__ l
   }
 }
 
-__global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict__ logits, int E, int K,
-                                                       const __half* __restrict__ x,
-                                                       const __half* __restrict__ g, int H, int* ids,
-                                                       __half* weights, __half* shared_w) {
-  extern __shared__ float vals[];  // E logits of this token
-  const int tok = blockIdx.x;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  pdl_launch_dependents();
-  pdl_wait_primary();
-  if (warp == 0) {
-    float sel_v = 0.f;  // lane r keeps the r-th selected logit
-    int sel_i = 0;
-    if (E <= 32 * kRouteLaneVals && K <= 32) {
-      route_select_sorted(logits + (size_t)tok * E, E, K, lane, &sel_v, &sel_i);
-    } else {
-    for (int i = lane; i < E; i += 32) vals[i] = __half2float(logits[(size_t)tok * E + i]);
+// Top-k selection, fp32 softmax of the selected logits and their ids, by
+// one warp for one token: lg = the token's E logits, ids_t / w_t its K
+// outputs, vals = E + 64 floats of this warp's shared memory.
+__device__ __forceinline__ void route_warp(const __half* __restrict__ lg, int E, int K, int lane, int* ids_t,
+                                           __half* w_t, float* vals) {
+  float sel_v = 0.f;  // lane r keeps the r-th selected logit
+  int sel_i = 0;
+  if (E <= 32 * kRouteLaneVals && K <= 32) {
+    route_select_sorted(lg, E, K, lane, &sel_v, &sel_i);
+  } else {
+    for (int i = lane; i < E; i += 32) vals[i] = __half2float(lg[i]);
     __syncwarp();
     // Each lane tracks the best of its own strided elements.
     auto lane_best = [&](float* bv, int* bi) {
@@ -657,31 +651,45 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
       }
       __syncwarp();
       if (r == 31 && K > 32) {  // lanes now hold selections 0..31: emit them before reuse
-        ids[(size_t)tok * K + lane] = sel_i;
+        ids_t[lane] = sel_i;
         vals[E + lane] = sel_v;  // park the value for the softmax
       }
     }
+  }
+  // softmax over the K selected logits (the first is the largest)
+  __syncwarp();
+  if (K > 32) {
+    if (lane < K - 32) {
+      ids_t[32 + lane] = sel_i;
+      vals[E + 32 + lane] = sel_v;
     }
-    // softmax over the K selected logits (the first is the largest)
-    __syncwarp();
-    if (K > 32) {
-      if (lane < K - 32) {
-        ids[(size_t)tok * K + 32 + lane] = sel_i;
-        vals[E + 32 + lane] = sel_v;
-      }
-    } else if (lane < K) {
-      ids[(size_t)tok * K + lane] = sel_i;
-      vals[E + lane] = sel_v;
-    }
-    __syncwarp();
-    const float mx = vals[E];
-    float e0 = lane < K ? expf(vals[E + lane] - mx) : 0.f;
-    float e1 = lane + 32 < K ? expf(vals[E + 32 + lane] - mx) : 0.f;
-    float sum = e0 + e1;
+  } else if (lane < K) {
+    ids_t[lane] = sel_i;
+    vals[E + lane] = sel_v;
+  }
+  __syncwarp();
+  const float mx = vals[E];
+  float e0 = lane < K ? expf(vals[E + lane] - mx) : 0.f;
+  float e1 = lane + 32 < K ? expf(vals[E + 32 + lane] - mx) : 0.f;
+  float sum = e0 + e1;
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    if (lane < K) weights[(size_t)tok * K + lane] = __float2half_rn(e0 / sum);
-    if (lane + 32 < K) weights[(size_t)tok * K + 32 + lane] = __float2half_rn(e1 / sum);
+  for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+  if (lane < K) w_t[lane] = __float2half_rn(e0 / sum);
+  if (lane + 32 < K) w_t[32 + lane] = __float2half_rn(e1 / sum);
+}
+
+__global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict__ logits, int E, int K,
+                                                       const __half* __restrict__ x,
+                                                       const __half* __restrict__ g, int H, int* ids,
+                                                       __half* weights, __half* shared_w) {
+  extern __shared__ float vals[];  // E logits of this token
+  const int tok = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  if (warp == 0) {
+    route_warp(logits + (size_t)tok * E, E, K, lane, ids + (size_t)tok * K, weights + (size_t)tok * K, vals);
   } else if (g != nullptr) {
     float acc = 0.f;
     const __half* xr = x + (size_t)tok * H;
@@ -705,6 +713,108 @@ __global__ void __launch_bounds__(64) moe_route_kernel(const __half* __restrict_
       shared_w[tok] = __float2half_rn(1.0f / (1.0f + expf(-v)));
     }
   }
+}
+
+// The router's F.linear and the routing in one launch (qwen_moe.py:386-416,
+// 505-509).  Every CTA computes rows of logits[t][r] = fp16(x_t . W_r) with
+// fp32 sums of the fp16 products (rows 0..E-1 the router, row E the shared
+// expert's gate when g is given); then each CTA counts itself done on a
+// global counter.  The last one (no CTA waits for another) selects each
+// token's top-k with route_warp, writes the softmax weights and
+// sigmoid(logits[t][E]), and sets the counter back to 0 for the next call.
+// Logits are read through L2 (ld.global.cg): an earlier call's last CTA may
+// have left the same addresses in this SM's L1.
+constexpr int kRouterWarps = 8;
+constexpr int kRouterRowsPerCta = kRouterWarps / 2;  // two warps per row, one half of H each
+constexpr int kRouterMaxTokens = 16;
+
+template <int TB>  // token bucket: 1, 4 or 16 (ntok <= TB)
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    moe_router_kernel(const __half* __restrict__ x, int ntok, int H, const __half* __restrict__ w, int E,
+                      const __half* __restrict__ g, int K, __half* logits, int* ids, __half* weights,
+                      __half* shared_w, unsigned int* counter) {
+  extern __shared__ float scratch[];  // per warp: E + 64 floats, then E + 8 halves of logits
+  __shared__ float part[kRouterWarps][TB];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rows = E + (g ? 1 : 0);
+  const int ld = E + 1;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  {
+    const int r = blockIdx.x * kRouterRowsPerCta + (warp >> 1);
+    const int half = warp & 1;
+    float acc[TB];
+#pragma unroll
+    for (int b = 0; b < TB; ++b) acc[b] = 0.f;
+    if (r < rows) {
+      const int hh = H / 2;
+      const __half* wr = (r < E ? w + (size_t)r * H : g) + half * hh;
+      const __half* xr = x + half * hh;
+      // all of the warp's weight loads in flight at once for one token
+#pragma unroll(TB == 1 ? 8 : (TB == 4 ? 2 : 1))
+      for (int j = lane * 8; j < hh; j += 32 * 8) {
+        float wf[8];
+        const uint4 wv = *reinterpret_cast<const uint4*>(wr + j);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(u32_as_h2(ww[q]));
+          wf[2 * q] = f.x;
+          wf[2 * q + 1] = f.y;
+        }
+#pragma unroll
+        for (int b = 0; b < TB; ++b) {
+          if (b < ntok) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xr + (size_t)b * H + j);
+            const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 f = __half22float2(u32_as_h2(xs[q]));
+              acc[b] = fmaf(f.x, wf[2 * q], fmaf(f.y, wf[2 * q + 1], acc[b]));
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < TB; ++b) {
+      float v = acc[b];
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+      if (lane == 0) part[warp][b] = v;
+    }
+    __syncthreads();
+    // the two halves of each row, added in a fixed order
+    if (threadIdx.x < kRouterRowsPerCta * TB) {
+      const int rr = threadIdx.x / TB;
+      const int b = threadIdx.x % TB;
+      const int row = blockIdx.x * kRouterRowsPerCta + rr;
+      if (row < rows && b < ntok)
+        logits[(size_t)b * ld + row] = __float2half_rn(part[2 * rr][b] + part[2 * rr + 1][b]);
+    }
+  }
+  __threadfence();  // this thread's logits before the CTA counts itself done
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* vals = scratch + warp * (E + 64);
+  __half* lg = reinterpret_cast<__half*>(scratch + kRouterWarps * (E + 64)) + warp * (E + 8);
+  for (int b = warp; b < ntok; b += kRouterWarps) {
+    for (int i = lane; i < rows; i += 32) lg[i] = __ldcg(logits + (size_t)b * ld + i);
+    __syncwarp();
+    route_warp(lg, E, K, lane, ids + (size_t)b * K, weights + (size_t)b * K, vals);
+    if (g != nullptr && lane == 0) {
+      const float v = __half2float(lg[E]);
+      shared_w[b] = __float2half_rn(1.0f / (1.0f + expf(-v)));
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = 0u;
 }
 
 }  // namespace gdsq

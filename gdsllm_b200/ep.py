@@ -56,7 +56,8 @@ class ExpertParallelMoE:
             raise ValueError(f"rank {self.rank} holds experts [{layer.expert_first}, "
                              f"{layer.expert_first + layer.num_local}), expected [{first}, {first + count})")
         self.partial = partial or moe.moe_partial
-        self.router = router or moe.route
+        # default: the fused router kernel (deterministic, so every rank routes alike)
+        self.router = router or (lambda x2d, _w, k, _sg: moe.route_fused(x2d, self.layer, k))
         self.allreduce = allreduce  # in-place sum of the fp32 partial; None -> NCCL
 
     def forward(self, x: torch.Tensor, out32: Optional[torch.Tensor] = None,

@@ -19,7 +19,7 @@ extension.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Optional, Tuple
 
 import torch
@@ -47,6 +47,7 @@ class MoeLayer:
     expert_total: Optional[int] = None
     shared: Optional[Tuple[Stack, Stack, Stack]] = None
     shared_gate: Optional[torch.Tensor] = None
+    _router: Optional["FusedRouter"] = field(default=None, repr=False, compare=False)
 
     @property
     def num_local(self) -> int:
@@ -77,6 +78,62 @@ def route(x2d: torch.Tensor, router: torch.Tensor, top_k: int, shared_gate: Opti
     logits = F.linear(x2d, router)
     g = None if shared_gate is None else shared_gate.reshape(-1).contiguous()
     return _ext().moe_route(logits, top_k, x2d if g is not None else None, g)
+
+
+ROUTER_MAX_EXPERTS, ROUTER_MAX_TOP_K = 512, 32
+# The kernel takes up to 16 tokens; from 5 on, cuBLAS's F.linear + the route
+# kernel is faster (config 4 at 8 tokens: 435 vs 346 tok/s), so route_fused
+# uses the fused kernel for at most 4.
+ROUTER_MAX_TOKENS = 4
+
+
+class FusedRouter:
+    """The router GEMV and the routing in one launch (gdsq_moe_router): no
+    F.linear.  The logits are this build's fused fp16 GEMV of x and the
+    router (fp32 sums of the fp16 products, rounded once, as F.linear
+    rounds its output), so a near-tie at the top-k boundary can resolve
+    differently from cuBLAS's logits; the selection is the exact top-k of
+    ``self.logits``.  One instance per call sequence on a stream (it owns
+    the kernel's completion counter)."""
+
+    def __init__(self, router: torch.Tensor, shared_gate: Optional[torch.Tensor] = None):
+        self.router = router.contiguous()
+        self.shared_gate = None if shared_gate is None else shared_gate.reshape(-1).contiguous()
+        self.experts, self.hidden = self.router.shape
+        self.counter = torch.zeros(1, dtype=torch.int32, device=router.device)
+        self.logits = None
+
+    @staticmethod
+    def fits(router: torch.Tensor, top_k: int, tokens: int) -> bool:
+        return (router.shape[0] <= ROUTER_MAX_EXPERTS and top_k <= ROUTER_MAX_TOP_K and
+                1 <= tokens <= ROUTER_MAX_TOKENS and router.shape[1] % 512 == 0)
+
+    def __call__(self, x2d: torch.Tensor, top_k: int):
+        from . import capi
+        b = x2d.shape[0]
+        x2d = x2d.contiguous()
+        if self.logits is None or self.logits.shape[0] < b:
+            self.logits = torch.empty(b, self.experts + 1, dtype=torch.float16, device=x2d.device)
+        ids = torch.empty(b, top_k, dtype=torch.int32, device=x2d.device)
+        w = torch.empty(b, top_k, dtype=torch.float16, device=x2d.device)
+        sw = None if self.shared_gate is None else torch.empty(b, dtype=torch.float16, device=x2d.device)
+        capi.check(capi.lib().gdsq_moe_router(
+            x2d.data_ptr(), b, self.hidden, self.router.data_ptr(), self.experts,
+            None if self.shared_gate is None else self.shared_gate.data_ptr(), top_k, self.logits.data_ptr(),
+            ids.data_ptr(), w.data_ptr(), None if sw is None else sw.data_ptr(), self.counter.data_ptr(),
+            torch.cuda.current_stream(x2d.device).cuda_stream), "gdsq_moe_router")
+        return ids, w, sw
+
+
+def route_fused(x2d: torch.Tensor, layer: "MoeLayer", top_k: int):
+    """``route`` through the layer's FusedRouter when its shapes fit (else
+    ``route``): (ids, weights, shared weight or None)."""
+    sg = layer.shared_gate if layer.shared is not None else None
+    if not FusedRouter.fits(layer.router, top_k, x2d.shape[0]):
+        return route(x2d, layer.router, top_k, sg)
+    if layer._router is None:
+        layer._router = FusedRouter(layer.router, sg)
+    return layer._router(x2d, top_k)
 
 
 def _ext():
@@ -117,11 +174,12 @@ def finish(y32: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
 
 def moe_mlp_decode(x: torch.Tensor, layer: MoeLayer, top_k: int = 10, add_residual: bool = False) -> torch.Tensor:
     """One MoE MLP on one GPU: x (B, S, hidden) or (B, hidden) fp16.  Three
-    launches after the router's F.linear: route, gate/up, down (clamped fp16).
+    launches: router + route (one kernel, ``route_fused``), gate/up, down
+    (clamped fp16).
     ``add_residual`` returns x + moe(x) (the caller's residual add, in the
     same fp16 roundings) from the down launch itself."""
     x2d = x.reshape(-1, x.shape[-1])
-    ids, weights, sw = route(x2d, layer.router, top_k, layer.shared_gate if layer.shared is not None else None)
+    ids, weights, sw = route_fused(x2d, layer, top_k)
     y = moe_partial(x2d, ids, weights, layer, shared_weights=sw, out_fp32=False, clamp=True,
                     residual=x2d.contiguous() if add_residual else None)
     return y.view(x.shape)

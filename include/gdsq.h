@@ -293,6 +293,21 @@ GDSQ_API int gdsq_moe_route(const void* logits, int num_tokens, int num_experts,
                             const void* shared_gate, int hidden_dim, int32_t* expert_ids, void* route_weights,
                             void* shared_weights, void* stream);
 
+/* The router's F.linear and gdsq_moe_route in one launch (qwen_moe.py:
+ * 386-416, 505-509): logits [num_tokens][num_experts + 1] fp16 = x .
+ * router_weight^T (fp32 sums of the fp16 products, rounded once; column
+ * num_experts holds x . shared_gate when shared_gate is given), then the
+ * top_k ids, softmax weights and the shared gate's sigmoid as
+ * gdsq_moe_route writes them.  The CTAs count themselves done on `counter`
+ * (one zero-initialised uint32 per call sequence on a stream; the last CTA
+ * routes and sets it back to 0).  num_tokens <= 16, num_experts <= 512,
+ * top_k <= 32, hidden_dim % 512 == 0; x, router_weight [num_experts]
+ * [hidden_dim] and shared_gate [hidden_dim] fp16, 16-byte aligned. */
+GDSQ_API int gdsq_moe_router(const void* x, int num_tokens, int hidden_dim, const void* router_weight,
+                             int num_experts, const void* shared_gate, int top_k, void* logits,
+                             int32_t* expert_ids, void* route_weights, void* shared_weights, unsigned int* counter,
+                             void* stream);
+
 /* ---- Decode step (batch 1, position in device memory) --------------------
  * The work of one LLaMA decode position around the fused GEMVs, so that a
  * whole token can be captured as one CUDA graph.  No reference launcher:

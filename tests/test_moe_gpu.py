@@ -257,7 +257,7 @@ def test_moe_layer_decode_matches_reference_layer(cuda):
                          shared=sdev, shared_gate=sgate.to(cuda))
     x = synth.activations(1, hidden, seed=6).view(1, 1, hidden)
     y = moe.moe_mlp_decode(x.to(cuda), layer, top_k)
-    ids, w, _ = moe.route(x.view(1, hidden).to(cuda), layer.router, top_k, layer.shared_gate)
+    ids, w, _ = moe.route_fused(x.view(1, hidden).to(cuda), layer, top_k)  # the routing moe_mlp_decode used
     torch.cuda.synchronize()
     ref = oracle.moe_mlp_reference(x.view(1, hidden).numpy(), ids.cpu().numpy(), w.cpu().numpy(), *cpu, group,
                                    shared=scpu, shared_gate_w=sgate.numpy())
@@ -356,3 +356,49 @@ def test_moe_route_kernel_matches_torch_topk(gdsq, cuda, ntok, experts, top_k):
         assert torch.equal(lg[t, ids[t].long().cpu()], tv[t].float().cpu()), "order differs from torch.topk"
     assert (w.float() - tw.float()).abs().max().item() <= 2 * 2 ** -11
     assert (sw.float() - tsw.float()).abs().max().item() <= 2 * 2 ** -11
+
+
+@pytest.mark.parametrize("ntok,experts,top_k,shared", [(1, 512, 10, True), (8, 512, 10, True), (16, 64, 7, False),
+                                                       (3, 33, 1, True)])
+def test_fused_router_matches_linear_and_route(gdsq, cuda, ntok, experts, top_k, shared):
+    """gdsq_moe_router: logits within an fp16 ulp of the fp64 product (fp32
+    sums, one rounding), and exactly the ids, weights and
+    shared gate that gdsq_moe_route gives on those logits; twice in a row
+    (the completion counter resets itself)."""
+    from gdsllm_b200 import moe
+    hidden = 4096
+    g = torch.Generator().manual_seed(ntok * 100 + experts)
+    router = (torch.randn(experts, hidden, generator=g) / hidden ** 0.5).half().to(cuda)
+    sgate = (torch.randn(hidden, generator=g) / hidden ** 0.5).half().to(cuda) if shared else None
+    x = synth.activations(ntok, hidden, seed=ntok + 5).to(cuda)
+    fr = moe.FusedRouter(router, sgate)  # called directly: every token count the kernel takes (<= 16)
+    for _ in range(2):
+        ids, w, sw = fr(x, top_k)
+        lg = fr.logits[:ntok]
+        # against the fp64 product: one fp16 rounding of an fp32 sum (cuBLAS's
+        # F.linear may reduce in lower precision, so it is not the yardstick)
+        exact = x.double() @ router.double().T
+        err = (lg[:, :experts].double() - exact).abs()
+        assert (err <= exact.abs() * 2 ** -10 + 2 ** -24 * 4096).all(), err.max().item()
+        if shared:
+            ex_g = x.double() @ sgate.double()
+            assert ((lg[:, experts].double() - ex_g).abs() <= ex_g.abs() * 2 ** -10 + 2 ** -14).all()
+        ids2, w2, sw2 = gdsq_route_on(lg[:, :experts].contiguous(), top_k, x if shared else None, sgate)
+        assert torch.equal(ids, ids2) and torch.equal(w, w2)
+        if shared:
+            # the fused kernel's gate is sigmoid of its own fp16 logit of x . g
+            expect = torch.sigmoid(lg[:, experts].float()).half()
+            assert (sw.float() - expect.float()).abs().max().item() <= 2 ** -10
+    torch.cuda.synchronize()
+    assert int(fr.counter.item()) == 0
+    assert capi_device_error() == 0
+
+
+def gdsq_route_on(logits, top_k, x, g):
+    from gdsllm_b200 import moe
+    return moe._ext().moe_route(logits, top_k, x, g)
+
+
+def capi_device_error():
+    from gdsllm_b200 import capi
+    return capi.device_error(0)
