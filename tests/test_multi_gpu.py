@@ -125,7 +125,7 @@ def _worker(rank, world, port, q):
         worst = 0.0
         for it, n in enumerate([8192, 1024, 24576, 8192, 8192]):
             t = synth.activations(1, n, seed=100 * it + rank).to(dev).view(-1)
-            ref = t.clone()
+            ref = t.float()  # fp32 sum: NCCL's fp16 sum of more than 2 ranks rounds once per step
             dist.all_reduce(ref)
             out = ar(t.clone())
             worst = max(worst, ((out.float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
@@ -143,7 +143,7 @@ def _worker(rank, world, port, q):
         for it in range(5):
             gin.copy_(synth.activations(1, 8192, seed=50 + it + 10 * rank).view(-1).to(dev))
             g.replay()
-            ref = gin.clone()
+            ref = gin.float()
             dist.all_reduce(ref)
             torch.cuda.synchronize()
             worst = max(worst, ((gout.float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
@@ -162,7 +162,7 @@ def _worker(rank, world, port, q):
                 ar(ys[i].view(-1), out=outs[i])
             torch.cuda.synchronize()
             for i in range(12):
-                ref = ys[i].view(-1).clone()
+                ref = ys[i].view(-1).float()
                 dist.all_reduce(ref)
                 worst = max(worst, ((outs[i].float() - ref.float()).abs() / (ref.float().abs() + 1)).max().item())
         capi.set_pdl(False)
@@ -173,7 +173,7 @@ def _worker(rank, world, port, q):
         # ---- row split with the all-reduce inside the GEMV epilogue ----
         from gdsllm_b200.p2p import PeerRowGemv
         fused = PeerRowGemv(k)
-        worst_f, agree = 0.0, True
+        worst_f, worst_n, agree = 0.0, 0.0, True
         cases = [("q4_0", synth.q4_0_weight, capi.gemv_q4_0, k, n), ("q8_0", synth.q8_0_weight, capi.gemv_q8_0, k, n),
                  ("q4_0", synth.q4_0_weight, capi.gemv_q4_0, 4096, 14336),
                  ("q4_0", synth.q4_0_weight, capi.gemv_q4_0, 1000, 2048)]
@@ -190,8 +190,9 @@ def _worker(rank, world, port, q):
                 y_n = layer_nccl(xl)
                 y_1 = full_gemv(wf, xf, nn, kk)
                 scale = y_1.float().abs().max().item()
-                worst_f = max(worst_f, (y_f.float() - y_1.float()).abs().max().item() / (scale + 1),
-                              (y_f.float() - y_n.float()).abs().max().item() / (scale + 1))
+                worst_f = max(worst_f, (y_f.float() - y_1.float()).abs().max().item() / (scale + 1))
+                # NCCL adds the fp16 partials in fp16 (one rounding per step beyond two ranks)
+                worst_n = max(worst_n, (y_f.float() - y_n.float()).abs().max().item() / (scale + 1))
                 both = [torch.empty_like(y_f) for _ in range(world)]
                 dist.all_gather(both, y_f)
                 agree = agree and all(torch.equal(both[0], b) for b in both)
@@ -218,6 +219,7 @@ def _worker(rank, world, port, q):
             worst_f = max(worst_f, (gy.float() - y_1.float()).abs().max().item() / (y_1.float().abs().max().item() + 1))
         del g
         res["fused"] = worst_f
+        res["fused_nccl"] = worst_n
         res["fused_agree"] = agree
         res["fused_err"] = capi.device_error(rank, clear=True)
         torch.cuda.synchronize()
@@ -250,7 +252,7 @@ def test_expert_and_tensor_parallel_on_gpus(world):
         assert res["col"] <= 2e-3 * res["col_scale"] + 1e-3, (rank, res)
         # row split: two fp16 partials added (one extra rounding each)
         assert res["row"] <= 4e-3 * res["row_scale"] + 2e-3, (rank, res)
-        # peer all-reduce: fp32 sum vs NCCL's fp16 sum, relative to the value
+        # peer all-reduce: its fp16 result vs the fp32 sum, relative to the value
         assert res["p2p"] <= 2e-3, (rank, res)
         assert res["p2p_err"] == 0, (rank, res)
         # two ranks: NCCL adds a + b as the word all-reduce does (same bits);
@@ -263,5 +265,6 @@ def test_expert_and_tensor_parallel_on_gpus(world):
         # fused row split: fp32 partials summed in rank order then one fp16
         # rounding, against the full single-GPU GEMV and the NCCL path
         assert res["fused"] <= 4e-3, (rank, res)
+        assert res["fused_nccl"] <= 2e-3 * world, (rank, res)
         assert res["fused_agree"], (rank, res)   # every rank holds the same bits
         assert res["fused_err"] == 0, (rank, res)
