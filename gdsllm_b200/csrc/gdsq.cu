@@ -548,14 +548,29 @@ int launch_fast_batch(const GemvParams& p, const DeviceInfo& dev, cudaStream_t s
   }
 }
 
-// Tensor-core batched GEMV (gemv_tcb.cuh): default for batch >= 5, where
-// the CUDA-core kernel's multiply-add work (linear in the batch) outgrows
-// the tensor-core kernel's fixed dequantization cost; GDSQ_GEMV_TCB=0 turns
-// it off, =1 uses it for every batch size.
+// Tensor-core batched GEMV (gemv_tcb.cuh): the default where the CUDA-core
+// kernel's multiply-add work (linear in the batch) outgrows the tensor-core
+// kernel's fixed dequantization cost (tcb_default); GDSQ_GEMV_TCB=0 turns it
+// off, =1 uses it for every batch size.
 int tcb_mode() {
   const char* e = getenv("GDSQ_GEMV_TCB");
   if (!e || !*e) return -1;
   return e[0] == '1' ? 1 : 0;
+}
+
+// The tensor-core kernel's time is nearly flat in the batch; the CUDA-core
+// kernel's grows with it, soonest for long rows and tall matrices.  Measured
+// per launch in graph chains with programmatic dependent launch (CUDA cores
+// vs tensor cores):
+//   K = 11008, batch 3: Q8_0 29.5 vs 23.7 us, Q4_0 and affine-Q4 equal;
+//              batch 4: Q4_0 38.9 vs 22.6, Q8_0 40.6 vs 23.8, affine 27.8 vs 23.2 us;
+//   N = 32000, batch 4: Q8_0 62.0 vs 53.8, affine 78.7 vs 52.1 us, Q4_0 equal;
+//   K = 4096 and N <= 11008, batch 4: within 5 % either way, except
+//              affine 4096 x 4096 (9.7 vs 12.3 us), so these stay on CUDA cores.
+bool tcb_default(int batch, int out_dim, int in_dim) {
+  if (batch >= 5) return true;
+  if (batch >= 3 && in_dim >= 8192) return true;
+  return batch == 4 && out_dim >= 16384;
 }
 
 // One CTA per SM.  Cost = the busiest CTA's chunks (plus two chunks' worth
@@ -777,7 +792,7 @@ int gemv_dispatch(int fmt, const void* w, const void* scales, const void* biases
     return launch_fast<kFmtQ8_0, 1, 0, true>(p, *dev, stream);
   }
   const int tcb = tcb_mode();
-  const bool use_tcb = shape_ok && (tcb == 1 || (tcb == -1 && batch >= 5));
+  const bool use_tcb = shape_ok && (tcb == 1 || (tcb == -1 && tcb_default(batch, out_dim, in_dim)));
   if (use_tcb) {
     if (fmt == kFmtQ4_0) return launch_tcb_batch<kFmtQ4_0, 0>(p, *dev, stream);
     if (fmt == kFmtQ8_0) return launch_tcb_batch<kFmtQ8_0, 0>(p, *dev, stream);
@@ -1329,6 +1344,8 @@ int gdsq_fused_gemv_group(int gguf_type, int count, const void* const* weights, 
   for (int m = 0; m < count; ++m) {
     if (out_dims[m] < 0) return fail(GDSQ_ERR_INVALID_VALUE, "gemv group: negative out_dim %d", out_dims[m]);
     fast = fast && weights[m] && aligned(weights[m], 16) && out_dims[m] > 0 && ys[m] && aligned(ys[m], 2);
+    // A matrix that the single GEMV would give to the tensor cores
+    fast = fast && !(tcb_mode() == -1 && tcb_default(batch, out_dims[m], in_dim));
   }
   if (count == 1 || !fast || tcb_mode() == 1) {
     // One launch per matrix (every check and path of the single GEMV).
