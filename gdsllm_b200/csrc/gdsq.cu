@@ -871,6 +871,11 @@ int make_moe_plan(int items, int C, const DeviceInfo& dev, MoePlan* out) {
       if (occ < 1) continue;
       const long long slots = (long long)dev.sms * occ;
       const long long ctas = (long long)items * cs;
+      // Down stage with more CTAs than one wave holds (batch 8: 1024 items
+      // of 44 chunks): a wider split or a deeper ring only adds CTAs or
+      // shared memory.  Config 4 at batch 8, cs:stages: 2:2 505 tok/s, 2:4
+      // 452, 4:2 430, 4:3 367, 8:2 379.
+      if (STAGE == 1 && !forced && ctas > slots && (cs > 2 || st > 2)) continue;
       double load;
       long long resident;
       int nclusters;
